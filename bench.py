@@ -1,0 +1,361 @@
+"""Decode-attention benchmark for the STAR-KV compressed-KV layer on B200.
+
+Workload: one decode step of one STAR-KV attention layer —
+batch 16, 32768 cached tokens (+1 appended), 32 MHA heads x 128, ragged K
+ranks in {16..96} (int8 per-channel codes), 8 V blocks of 4 heads with ranks
+in {64,128,192} (int4 per-token groups of 32), fp16 compute.  A step appends the
+new token's latents (quantise + in-place write) and runs the fused decode
+attention over all 32769 slots, producing the per-head outputs fed to o_proj.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun, one rank per GPU): each rank owns a contiguous range of heads
+(whole V blocks) and one NCCL all-gather collects the per-head outputs.  The
+JSON line's ``value`` is whole-job decode tokens/s (batch / step time, max over
+ranks); ``e2e`` is the same metric through the public step API with host
+buffers (pinned H2D of the step's query and latents, D2H of the output).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "star-kv_b200"), ROOT]
+
+import numpy as np  # noqa: E402
+
+METRIC = "decode attn tokens/s & µs/layer at ctx 32K, batch 16; HBM GB/s vs peak"
+UNIT = "tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic():
+    """DRAM bytes per K-kernel launch from the committed ncu summary (None if absent)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "k_logits_c1_traffic.json")) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        if not getattr(self, "lines", None):
+            return None
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            f = [x.strip() for x in l.split(",")]
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except Exception:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- sharding
+def shard_spec(spec, rank: int, world: int):
+    """Heads of rank `rank`: a contiguous range of whole V blocks."""
+    import copy
+    nb = spec.num_v_blocks
+    if nb % world:
+        raise SystemExit(f"{nb} V blocks do not split over {world} GPUs")
+    per = nb // world
+    b0, b1 = rank * per, (rank + 1) * per
+    kv0 = sum(spec.v_block_kv[:b0])
+    kv1 = sum(spec.v_block_kv[:b1])
+    qpk = spec.num_q_heads // spec.num_kv_heads
+    sub = copy.deepcopy(spec)
+    sub.k_ranks = spec.k_ranks[kv0:kv1]
+    sub.v_ranks = spec.v_ranks[b0:b1]
+    sub.v_block_kv = spec.v_block_kv[b0:b1]
+    sub.num_kv_heads = kv1 - kv0
+    sub.num_q_heads = (kv1 - kv0) * qpk
+    return sub
+
+
+# ---------------------------------------------------------------- CPU arm
+def cpu_sample(spec, seed: int = 0):
+    """Time the oracle port (numpy, fp32) on one sequence of the workload."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import copy
+
+    import starkv_oracle as O
+    from starkv.synthetic import make_layer
+    one = copy.deepcopy(spec)
+    one.batch = 1
+    data = make_layer(one, seed=seed)
+    t0 = time.perf_counter()
+    O.layer_reference(data, dtype=np.float32)
+    return time.perf_counter() - t0
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, spec):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ts = []
+    for i in range(args.warmup + args.steps):
+        t = cpu_sample(spec, seed=i)
+        if i >= args.warmup:
+            ts.append(t)
+    t = sum(ts) / len(ts)
+    v = 1.0 / t
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(spec, args.gpus),
+        "cpu_baseline": {"value": v, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
+                         "sample": "one sequence (batch 1 of 16) of the config-1 step: all 32 heads over "
+                                   "32769 slots, numpy fp32 oracle port of the reference eager path"},
+        "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(spec, n):
+    return {
+        "workload": (f"{spec.name}: one decode step of one STAR-KV attention layer (append + fused attention), "
+                     f"B={spec.batch}, ctx {spec.context}+1, {spec.num_q_heads}q/{spec.num_kv_heads}kv heads x 128, "
+                     + ("int8 K / int4 V latents" if spec.quantized else f"{spec.dtype} latents")),
+        "batch": spec.batch, "context": spec.context, "k_ranks": spec.k_ranks, "v_ranks": spec.v_ranks,
+        "parallelism": f"heads{n}" if n > 1 else "single",
+        "l2": "inputs larger than L2 (compressed cache %.2f GB per step)" % (spec.compressed_bytes_per_step() / 1e9),
+    }
+
+
+# ---------------------------------------------------------------- GPU arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="c1")
+    ap.add_argument("--context", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    from starkv.synthetic import make_spec
+    over = {}
+    if args.context:
+        over["context"] = args.context
+    if args.batch:
+        over["batch"] = args.batch
+    spec = make_spec(args.config, seed=0, **over)
+
+    if args.impl == "reference":
+        run_reference(args, spec)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus and world > 1:
+        args.gpus = world
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    from starkv import ops
+    from starkv.harness import device_layer
+
+    sub = shard_spec(spec, rank, world) if world > 1 else spec
+    st, _, _ = device_layer(sub, dev, seed=1 + rank)
+    layer = st.layer
+    layer.num_splits = args.splits
+    L = sub.context
+    B, hq = sub.batch, sub.num_q_heads
+    out = torch.empty(B, hq, 128, dtype=st.q.dtype, device=dev)
+    gathered = torch.empty(world, B, hq, 128, dtype=st.q.dtype, device=dev) if world > 1 else None
+
+    def step(events=None):
+        layer.cache.length = L                      # the step rewrites slot L and attends 0..L
+        layer.step(st.q, st.k_new, st.v_new, out=out, events=events)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert ops.read_device_error(device=dev) == 0
+
+    K = args.steps
+    kev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0.record()
+        for i in range(K):
+            step(kev[i])
+        t1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1) / K
+    k_ms = sum(e[0].elapsed_time(e[1]) for e in kev) / K
+    v_ms = sum(e[1].elapsed_time(e[2]) for e in kev) / K
+    c_ms = sum(e[2].elapsed_time(e[3]) for e in kev) / K
+    if world > 1:
+        t = torch.tensor([ms, k_ms, v_ms, c_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, k_ms, v_ms, c_ms = t.tolist()
+
+    # ---- e2e through the public step API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        hq_pin = st.q.cpu().pin_memory()
+        hk_pin = st.k_new.cpu().pin_memory()
+        hv_pin = st.v_new.cpu().pin_memory()
+        hout = torch.empty(world * B * hq * 128 if world > 1 else B * hq * 128, dtype=out.dtype).pin_memory()
+        dq, dk, dv = torch.empty_like(st.q), torch.empty_like(st.k_new), torch.empty_like(st.v_new)
+
+        def e2e_step():
+            dq.copy_(hq_pin, non_blocking=True)
+            dk.copy_(hk_pin, non_blocking=True)
+            dv.copy_(hv_pin, non_blocking=True)
+            layer.cache.length = L
+            layer.step(dq, dk, dv, out=out)
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, out)
+                hout.copy_(gathered.view(-1), non_blocking=True)
+            else:
+                hout.copy_(out.view(-1), non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(K):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        ems = e0.elapsed_time(e1) / K
+        if world > 1:
+            t = torch.tensor([ems], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = t.item()
+        h2d = (hq_pin.numel() + hk_pin.numel() + hv_pin.numel()) * hq_pin.element_size()
+        d2h = hout.numel() * hout.element_size()
+        e2e = {"value": spec.batch / (ems / 1e3), "unit": UNIT, "ms_per_step": ems,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+               "api": "starkv.layer.DecodeLayer.step (C ABI starkv_append + starkv_decode_attention)"}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    peak, peak_kind = measured_peak()
+    T = sub.tokens
+    step_bytes = spec.compressed_bytes_per_step()                       # whole job
+    rank_bytes = sub.compressed_bytes_per_step()
+    k_bytes = sub.batch * T * sub.k_rank_total + sub.batch * sub.k_rank_total * 2
+    v_bytes = rank_bytes - k_bytes
+    k_gbs = k_bytes / (k_ms / 1e3) / 1e9
+    traffic = ncu_traffic()
+    roofline = {"kernel": "k_logits_kernel<int8_t,true> (fused K reconstruction + RoPE + q.k + split softmax)",
+                "bound": "hbm", "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak,
+                "peak_kind": peak_kind,
+                "traffic": (traffic or {}).get("dram_bytes_per_launch_full_size"),
+                "algorithmic_bytes_per_launch": k_bytes, "avg_launch_ms": k_ms}
+    line = {
+        "metric": METRIC, "value": spec.batch / (ms / 1e3), "unit": UNIT, "n_gpus": world,
+        "steps": K, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": workload_config(spec, world),
+        "us_per_layer": ms * 1e3,
+        "hbm_gbs_per_gpu": rank_bytes / (ms / 1e3) / 1e9,
+        "hbm_frac_step": (rank_bytes / (ms / 1e3) / 1e9) / peak,
+        "kernels_ms": {"k_logits": k_ms, "v_latent": v_ms, "combine": c_ms},
+        "v_kernel_gbs": v_bytes / (v_ms / 1e3) / 1e9,
+        "roofline": roofline,
+        "gpu_launches": 5 * K,
+        "e2e": e2e,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu:
+        t = cpu_sample(spec)
+        line["cpu_baseline"] = {"value": 1.0 / t, "unit": UNIT, "cores": cpu_cores(), "kind": "port",
+                                "sample": "one sequence (batch 1 of 16) of the same step: all heads over all "
+                                          "slots, numpy fp32 oracle port of the reference eager path"}
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

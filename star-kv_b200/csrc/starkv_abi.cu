@@ -1,0 +1,526 @@
+// starkv_abi.cu — the extern "C" entry points of libstarkv.so (declared in
+// include/starkv.h): validation, launch geometry, workspace carving and the
+// kernel launches of the decode step.  No entry point allocates device memory.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <type_traits>
+
+#include "common.cuh"
+#include "k_logits.cuh"
+#include "quant.cuh"
+#include "sm100.cuh"
+#include "v_latent.cuh"
+
+using namespace starkv;
+
+namespace {
+
+thread_local char g_last_error[256] = "";
+
+int fail_launch() {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return STARKV_OK;
+  snprintf(g_last_error, sizeof(g_last_error), "%s", cudaGetErrorString(e));
+  return STARKV_ERR_LAUNCH;
+}
+
+int set_error(int code, const char* msg) {
+  snprintf(g_last_error, sizeof(g_last_error), "%s", msg);
+  return code;
+}
+
+constexpr int kMaxDevices = 64;
+
+int device_sm_count(int* dev_out) {
+  static int sm_count[kMaxDevices] = {0};
+  static int is_sm100[kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+  if (sm_count[dev] == 0) {
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) return -1;
+    is_sm100[dev] = (prop.major == 10 && prop.minor == 0) ? 1 : -1;
+    sm_count[dev] = prop.multiProcessorCount;
+  }
+  if (dev_out) *dev_out = dev;
+  return is_sm100[dev] > 0 ? sm_count[dev] : 0;
+}
+
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device).
+template <typename K>
+int ensure_smem(K kernel, size_t bytes, int slot) {
+  static size_t configured[8][kMaxDevices] = {{0}};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= kMaxDevices || slot < 0 || slot >= 8) return STARKV_ERR_INVALID;
+  if (configured[slot][dev] >= bytes) return STARKV_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
+    return fail_launch();
+  configured[slot][dev] = bytes;
+  return STARKV_OK;
+}
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+int max_k_rank(const starkv_layout& l) {
+  int m = 0;
+  for (int h = 0; h < l.num_kv_heads; ++h) m = l.k_rank[h] > m ? l.k_rank[h] : m;
+  return m;
+}
+int max_v_rank(const starkv_layout& l) {
+  int m = 0;
+  for (int j = 0; j < l.num_v_blocks; ++j) m = l.v_rank[j] > m ? l.v_rank[j] : m;
+  return m;
+}
+int k_elem_bytes(const starkv_layout& l) { return l.quantized ? 1 : dtype_bytes(l.latent_dtype); }
+
+// K-path geometry: heads per CTA (G) and staging stages (S) that fit shared memory.
+struct KGeom {
+  int G, S, rmax;
+  size_t smem;
+};
+
+KGeom k_geometry(const starkv_layout& l) {
+  KGeom g;
+  g.rmax = max_k_rank(l);
+  const int xb = k_elem_bytes(l);
+  const int Hq = l.num_q_heads;
+  for (int G = 4; G >= 1; G >>= 1) {
+    if (Hq % G) continue;
+    for (int S = 4; S >= 2; --S) {
+      const size_t bytes = k_smem_bytes(G, S, g.rmax, xb);
+      if (bytes <= 227 * 1024) {
+        g.G = G;
+        g.S = S;
+        // at least 80 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
+        g.smem = bytes < 80 * 1024 ? 80 * 1024 : bytes;
+        return g;
+      }
+    }
+  }
+  g.G = 0;
+  g.S = 0;
+  g.smem = 0;
+  return g;
+}
+
+int auto_splits(const starkv_layout& l, int T, int sms) {
+  const KGeom g = k_geometry(l);
+  if (g.G == 0 || T <= 0) return 1;
+  const int ntiles = (T + 127) / 128;
+  const long base = (long)l.batch * (l.num_q_heads / g.G);
+  const int per_sm = g.smem > 113 * 1024 ? 1 : 2;
+  const long slots = (long)(sms > 0 ? sms : 148) * per_sm;
+  int best = 1;
+  double best_t = 1e30;
+  for (int ns = 1; ns <= ntiles && ns <= 128; ++ns) {
+    const int tiles = (ntiles + ns - 1) / ns;
+    const long ctas = base * ns;
+    const long waves = (ctas + slots - 1) / slots;
+    const double t = (double)waves * (tiles + 1.5);  // ~1.5 tiles of per-CTA fill/prologue
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = ns;
+    }
+  }
+  return best;
+}
+
+struct WsLayout {
+  size_t err, logits, stats, partial, rope, total;
+};
+
+WsLayout ws_layout(const starkv_layout& l, int T, int ns) {
+  WsLayout w;
+  const size_t BH = (size_t)l.batch * l.num_q_heads;
+  w.err = 0;
+  w.logits = 256;
+  w.stats = w.logits + align256(BH * T * sizeof(float));
+  w.partial = w.stats + align256(BH * ns * sizeof(float2));
+  w.rope = w.partial + align256(BH * ns * max_v_rank(l) * sizeof(float));
+  w.total = w.rope + align256((size_t)T * 64 * sizeof(float2));
+  return w;
+}
+
+int validate(const starkv_layout* lp) {
+  if (!lp) return set_error(STARKV_ERR_INVALID, "null layout");
+  const starkv_layout& l = *lp;
+  if (l.abi_version != STARKV_ABI_VERSION) return set_error(STARKV_ERR_INVALID, "layout ABI version mismatch");
+  if (l.batch <= 0 || l.num_q_heads <= 0 || l.num_kv_heads <= 0 || l.capacity <= 0)
+    return set_error(STARKV_ERR_INVALID, "non-positive batch/heads/capacity");
+  if (l.head_dim != STARKV_HEAD_DIM) return set_error(STARKV_ERR_UNSUPPORTED, "head_dim must be 128");
+  if (l.num_kv_heads > STARKV_MAX_KV_HEADS || l.num_v_blocks <= 0 || l.num_v_blocks > STARKV_MAX_V_BLOCKS)
+    return set_error(STARKV_ERR_UNSUPPORTED, "too many KV heads or V blocks");
+  if (l.num_q_heads % l.num_kv_heads) return set_error(STARKV_ERR_INVALID, "num_q_heads % num_kv_heads != 0");
+  if (l.latent_dtype < STARKV_F32 || l.latent_dtype > STARKV_BF16)
+    return set_error(STARKV_ERR_UNSUPPORTED, "latent dtype");
+  const int xb = k_elem_bytes(l);
+  int col = 0;
+  for (int h = 0; h < l.num_kv_heads; ++h) {
+    const int r = l.k_rank[h];
+    if (r <= 0 || r % 16 || r > STARKV_MAX_K_RANK)
+      return set_error(STARKV_ERR_UNSUPPORTED, "K rank must be a multiple of 16 in [16, 128]");
+    if (l.k_col[h] != col) return set_error(STARKV_ERR_INVALID, "k_col is not the prefix sum of k_rank");
+    col += r;
+    if ((l.k_offset[h] * xb) % 16 || (l.k_batch_stride[h] * xb) % 16 || l.k_offset[h] < 0)
+      return set_error(STARKV_ERR_INVALID, "K offsets / batch strides must be 16-byte multiples");
+    if (l.k_batch_stride[h] < (int64_t)l.capacity * r)
+      return set_error(STARKV_ERR_INVALID, "K batch stride smaller than capacity * rank");
+  }
+  if (col != l.k_rank_total) return set_error(STARKV_ERR_INVALID, "k_rank_total mismatch");
+  const int qpk = l.num_q_heads / l.num_kv_heads;
+  int vcol = 0, kv = 0;
+  for (int j = 0; j < l.num_v_blocks; ++j) {
+    const int r = l.v_rank[j];
+    if (r <= 0 || r % 32 || r > 256) return set_error(STARKV_ERR_UNSUPPORTED, "V rank must be a multiple of 32 in [32, 256]");
+    if (l.v_col[j] != vcol) return set_error(STARKV_ERR_INVALID, "v_col is not the prefix sum of v_rank");
+    if (l.v_first_kv[j] != kv || l.v_num_kv[j] <= 0) return set_error(STARKV_ERR_INVALID, "V blocks must tile the KV heads in order");
+    if (l.v_num_kv[j] * qpk > kVMaxHeads) return set_error(STARKV_ERR_UNSUPPORTED, "more than 8 query heads in a V block");
+    vcol += r;
+    kv += l.v_num_kv[j];
+  }
+  if (kv != l.num_kv_heads) return set_error(STARKV_ERR_INVALID, "V blocks do not cover the KV heads");
+  if (vcol != l.v_rank_total) return set_error(STARKV_ERR_INVALID, "v_rank_total mismatch");
+  if (k_geometry(l).G == 0) return set_error(STARKV_ERR_UNSUPPORTED, "K ranks too large for shared memory");
+  return STARKV_OK;
+}
+
+int check_device() {
+  const int sms = device_sm_count(nullptr);
+  if (sms < 0) return set_error(STARKV_ERR_LAUNCH, "no CUDA device");
+  if (sms == 0) return set_error(STARKV_ERR_DEVICE, "libstarkv kernels need an sm_100 (B200) device");
+  return STARKV_OK;
+}
+
+inline unsigned grid1d(int64_t n, int threads) {
+  int64_t b = (n + threads - 1) / threads;
+  if (b > 148 * 64) b = 148 * 64;
+  if (b < 1) b = 1;
+  return (unsigned)b;
+}
+
+template <typename XT, bool QUANT>
+int launch_k(const KParams& kp, const KGeom& g, cudaStream_t st) {
+  auto kern = k_logits_kernel<XT, QUANT>;
+  const int slot = QUANT ? 0 : (sizeof(XT) == 4 ? 1 : (std::is_same<XT, __half>::value ? 2 : 3));
+  int rc = ensure_smem(kern, g.smem, slot);
+  if (rc) return rc;
+  dim3 grid(kp.nsplit, kp.lay.num_q_heads / kp.G, kp.lay.batch);
+  kern<<<grid, kKThreads, g.smem, st>>>(kp);
+  return fail_launch();
+}
+
+int dispatch_k(const KParams& kp, const KGeom& g, cudaStream_t st) {
+  if (kp.lay.quantized) return launch_k<int8_t, true>(kp, g, st);
+  switch (kp.lay.latent_dtype) {
+    case STARKV_F16: return launch_k<__half, false>(kp, g, st);
+    case STARKV_BF16: return launch_k<__nv_bfloat16, false>(kp, g, st);
+    default: return launch_k<float, false>(kp, g, st);
+  }
+}
+
+template <typename LT, bool QUANT>
+int launch_v(const VParams& vp, int nsplit, cudaStream_t st) {
+  auto kern = v_latent_kernel<LT, QUANT>;
+  const size_t smem = v_smem_bytes(kVMaxHeads);
+  const int slot = 4 + (QUANT ? 0 : (sizeof(LT) == 4 ? 1 : (std::is_same<LT, __half>::value ? 2 : 3)));
+  int rc = ensure_smem(kern, smem, slot);
+  if (rc) return rc;
+  dim3 grid(nsplit, vp.lay.num_v_blocks, vp.lay.batch);
+  kern<<<grid, kVThreads, smem, st>>>(vp);
+  return fail_launch();
+}
+
+int dispatch_v(const VParams& vp, int nsplit, cudaStream_t st) {
+  if (vp.lay.quantized) return launch_v<uint8_t, true>(vp, nsplit, st);
+  switch (vp.lay.latent_dtype) {
+    case STARKV_F16: return launch_v<__half, false>(vp, nsplit, st);
+    case STARKV_BF16: return launch_v<__nv_bfloat16, false>(vp, nsplit, st);
+    default: return launch_v<float, false>(vp, nsplit, st);
+  }
+}
+
+int launch_rope(const float* inv_freq, int first, int count, float2* table, cudaStream_t st) {
+  if (count <= 0) return STARKV_OK;
+  const int64_t n = (int64_t)count * 64;
+  rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(inv_freq, first, count, table);
+  return fail_launch();
+}
+
+// Shared front half of decode / logits: validation + K-path parameters.
+int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp, KGeom& g) {
+  int rc = validate(lay);
+  if (rc) return rc;
+  if (!a || !a->q || !a->k_u || !a->k_cache || !a->inv_freq) return set_error(STARKV_ERR_INVALID, "null argument");
+  if (lay->quantized && !a->k_scales) return set_error(STARKV_ERR_INVALID, "quantised layout needs k_scales");
+  if (a->num_tokens <= 0 || a->num_tokens > lay->capacity)
+    return set_error(STARKV_ERR_INVALID, "num_tokens outside (0, capacity]");
+  rc = check_device();
+  if (rc) return rc;
+  g = k_geometry(*lay);
+  memset(&kp, 0, sizeof(kp));
+  kp.lay = *lay;
+  kp.q = a->q;
+  kp.k_u = a->k_u;
+  kp.k_cache = a->k_cache;
+  kp.k_scales = reinterpret_cast<const __half*>(a->k_scales);
+  kp.q_dtype = a->q_dtype;
+  kp.w_dtype = a->w_dtype;
+  kp.T = a->num_tokens;
+  kp.G = g.G;
+  kp.S = g.S;
+  kp.rmax = g.rmax;
+  return STARKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t starkv_layout_size(void) { return sizeof(starkv_layout); }
+
+int starkv_validate_layout(const starkv_layout* lay) { return validate(lay); }
+
+const char* starkv_last_error(void) { return g_last_error; }
+
+int32_t starkv_auto_splits(const starkv_layout* lay, int32_t num_tokens) {
+  if (validate(lay)) return 1;
+  const int sms = device_sm_count(nullptr);
+  return auto_splits(*lay, num_tokens, sms > 0 ? sms : 148);
+}
+
+int starkv_decode_workspace_size(const starkv_layout* lay, int32_t num_tokens, int32_t num_splits, size_t* bytes) {
+  int rc = validate(lay);
+  if (rc) return rc;
+  if (!bytes || num_tokens <= 0) return set_error(STARKV_ERR_INVALID, "bad arguments");
+  const int ns = num_splits > 0 ? num_splits : starkv_auto_splits(lay, num_tokens);
+  *bytes = ws_layout(*lay, num_tokens, ns).total;
+  return STARKV_OK;
+}
+
+int starkv_rope_table(const float* inv_freq, int32_t first, int32_t count, void* table, starkv_stream_t stream) {
+  if (!inv_freq || !table || first < 0 || count < 0) return set_error(STARKV_ERR_INVALID, "bad arguments");
+  int rc = check_device();
+  if (rc) return rc;
+  return launch_rope(inv_freq, first, count, reinterpret_cast<float2*>(table), (cudaStream_t)stream);
+}
+
+int starkv_quantize_prefill(const starkv_layout* lay, const void* k_lat, const void* v_lat, int32_t num_tokens,
+                            void* k_cache, void* k_scales, void* v_cache, void* v_params, starkv_stream_t stream) {
+  int rc = validate(lay);
+  if (rc) return rc;
+  if (!k_lat || !v_lat || !k_cache || !v_cache || num_tokens < 0 || num_tokens > lay->capacity)
+    return set_error(STARKV_ERR_INVALID, "bad arguments");
+  if (lay->quantized && (!k_scales || !v_params)) return set_error(STARKV_ERR_INVALID, "null scales");
+  rc = check_device();
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const starkv_layout& l = *lay;
+  if (!l.quantized) return starkv_append(lay, k_lat, v_lat, num_tokens, 0, k_cache, k_scales, v_cache, v_params, stream);
+  dim3 kg(l.num_kv_heads, l.batch);
+  switch (l.latent_dtype) {
+    case STARKV_F16:
+      k_prefill_quant_kernel<__half><<<kg, 256, 0, st>>>(l, (const __half*)k_lat, num_tokens, (int8_t*)k_cache, (__half*)k_scales);
+      break;
+    case STARKV_BF16:
+      k_prefill_quant_kernel<__nv_bfloat16><<<kg, 256, 0, st>>>(l, (const __nv_bfloat16*)k_lat, num_tokens, (int8_t*)k_cache, (__half*)k_scales);
+      break;
+    default:
+      k_prefill_quant_kernel<float><<<kg, 256, 0, st>>>(l, (const float*)k_lat, num_tokens, (int8_t*)k_cache, (__half*)k_scales);
+  }
+  rc = fail_launch();
+  if (rc || num_tokens == 0) return rc;
+  const int64_t nthreads = (int64_t)l.batch * num_tokens * (l.v_rank_total / 32) * 32;
+  const unsigned grid = grid1d(nthreads, 256);
+  switch (l.latent_dtype) {
+    case STARKV_F16:
+      v_quant_kernel<__half><<<grid, 256, 0, st>>>(l, (const __half*)v_lat, num_tokens, 0, (uint8_t*)v_cache, (__half2*)v_params);
+      break;
+    case STARKV_BF16:
+      v_quant_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(l, (const __nv_bfloat16*)v_lat, num_tokens, 0, (uint8_t*)v_cache, (__half2*)v_params);
+      break;
+    default:
+      v_quant_kernel<float><<<grid, 256, 0, st>>>(l, (const float*)v_lat, num_tokens, 0, (uint8_t*)v_cache, (__half2*)v_params);
+  }
+  return fail_launch();
+}
+
+int starkv_append(const starkv_layout* lay, const void* k_lat, const void* v_lat, int32_t num_tokens,
+                  int32_t start_slot, void* k_cache, const void* k_scales, void* v_cache, void* v_params,
+                  starkv_stream_t stream) {
+  int rc = validate(lay);
+  if (rc) return rc;
+  if (!k_lat || !v_lat || !k_cache || !v_cache || num_tokens < 0 || start_slot < 0 ||
+      (int64_t)start_slot + num_tokens > lay->capacity)
+    return set_error(STARKV_ERR_INVALID, "bad arguments (slots beyond capacity?)");
+  if (lay->quantized && (!k_scales || !v_params)) return set_error(STARKV_ERR_INVALID, "null scales");
+  rc = check_device();
+  if (rc) return rc;
+  if (num_tokens == 0) return STARKV_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  const starkv_layout& l = *lay;
+  if (!l.quantized) {
+    const int64_t n = (int64_t)l.batch * num_tokens * (l.k_rank_total + l.v_rank_total);
+    const unsigned grid = grid1d(n, 256);
+    switch (l.latent_dtype) {
+      case STARKV_F16:
+        copy_append_kernel<__half><<<grid, 256, 0, st>>>(l, (const __half*)k_lat, (const __half*)v_lat, num_tokens, start_slot, (__half*)k_cache, (__half*)v_cache);
+        break;
+      case STARKV_BF16:
+        copy_append_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(l, (const __nv_bfloat16*)k_lat, (const __nv_bfloat16*)v_lat, num_tokens, start_slot, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache);
+        break;
+      default:
+        copy_append_kernel<float><<<grid, 256, 0, st>>>(l, (const float*)k_lat, (const float*)v_lat, num_tokens, start_slot, (float*)k_cache, (float*)v_cache);
+    }
+    return fail_launch();
+  }
+  const int64_t nk = (int64_t)l.batch * num_tokens * l.k_rank_total;
+  const int64_t nv = (int64_t)l.batch * num_tokens * (l.v_rank_total / 32) * 32;
+  switch (l.latent_dtype) {
+    case STARKV_F16:
+      k_append_quant_kernel<__half><<<grid1d(nk, 256), 256, 0, st>>>(l, (const __half*)k_lat, num_tokens, start_slot, (int8_t*)k_cache, (const __half*)k_scales);
+      v_quant_kernel<__half><<<grid1d(nv, 256), 256, 0, st>>>(l, (const __half*)v_lat, num_tokens, start_slot, (uint8_t*)v_cache, (__half2*)v_params);
+      break;
+    case STARKV_BF16:
+      k_append_quant_kernel<__nv_bfloat16><<<grid1d(nk, 256), 256, 0, st>>>(l, (const __nv_bfloat16*)k_lat, num_tokens, start_slot, (int8_t*)k_cache, (const __half*)k_scales);
+      v_quant_kernel<__nv_bfloat16><<<grid1d(nv, 256), 256, 0, st>>>(l, (const __nv_bfloat16*)v_lat, num_tokens, start_slot, (uint8_t*)v_cache, (__half2*)v_params);
+      break;
+    default:
+      k_append_quant_kernel<float><<<grid1d(nk, 256), 256, 0, st>>>(l, (const float*)k_lat, num_tokens, start_slot, (int8_t*)k_cache, (const __half*)k_scales);
+      v_quant_kernel<float><<<grid1d(nv, 256), 256, 0, st>>>(l, (const float*)v_lat, num_tokens, start_slot, (uint8_t*)v_cache, (__half2*)v_params);
+  }
+  return fail_launch();
+}
+
+int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* a, starkv_stream_t stream) {
+  KParams kp;
+  KGeom g;
+  int rc = prepare_k(lay, a, kp, g);
+  if (rc) return rc;
+  if (!a->v_cache || !a->v_u || !a->out || !a->workspace) return set_error(STARKV_ERR_INVALID, "null argument");
+  if (lay->quantized && !a->v_params) return set_error(STARKV_ERR_INVALID, "quantised layout needs v_params");
+  if (reinterpret_cast<uintptr_t>(a->workspace) % 256) return set_error(STARKV_ERR_INVALID, "workspace not 256-byte aligned");
+  const int T = a->num_tokens;
+  const int sms = device_sm_count(nullptr);
+  const int ns = a->num_splits > 0 ? a->num_splits : auto_splits(*lay, T, sms);
+  const WsLayout w = ws_layout(*lay, T, ns);
+  if (a->workspace_bytes < w.total) return set_error(STARKV_ERR_WORKSPACE, "workspace too small");
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+
+  const float2* rope = reinterpret_cast<const float2*>(a->rope_table);
+  if (!rope) {
+    rc = launch_rope(a->inv_freq, 0, T, reinterpret_cast<float2*>(ws + w.rope), st);
+    if (rc) return rc;
+    rope = reinterpret_cast<const float2*>(ws + w.rope);
+  }
+  const int ntiles = (T + 127) / 128;
+  const int tiles_per = (ntiles + ns - 1) / ns;
+  kp.rope = rope;
+  kp.mask = a->mask;
+  kp.logits = reinterpret_cast<float*>(ws + w.logits);
+  kp.stats = reinterpret_cast<float2*>(ws + w.stats);
+  kp.err = reinterpret_cast<int*>(ws + w.err);
+  kp.nsplit = ns;
+  kp.tps = tiles_per * 128;
+  const float log2e = 1.4426950408889634f;
+  kp.out_scale = a->scaling * log2e;
+  kp.mask_scale = log2e;
+  cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(a->events);
+  if (ev) cudaEventRecord(ev[0], st);
+  rc = dispatch_k(kp, g, st);
+  if (rc) return rc;
+  if (ev) cudaEventRecord(ev[1], st);
+
+  VParams vp;
+  memset(&vp, 0, sizeof(vp));
+  vp.lay = *lay;
+  vp.logits = kp.logits;
+  vp.stats = kp.stats;
+  vp.v_cache = a->v_cache;
+  vp.v_params = reinterpret_cast<const __half2*>(a->v_params);
+  vp.partial = reinterpret_cast<float*>(ws + w.partial);
+  vp.T = T;
+  vp.nsplit = ns;
+  vp.nsplit_k = ns;
+  vp.tps = kp.tps;
+  vp.rv_max = max_v_rank(*lay);
+  rc = dispatch_v(vp, ns, st);
+  if (rc) return rc;
+  if (ev) cudaEventRecord(ev[2], st);
+
+  CombineParams cp;
+  memset(&cp, 0, sizeof(cp));
+  cp.lay = *lay;
+  cp.partial = vp.partial;
+  cp.v_u = a->v_u;
+  cp.out = a->out;
+  cp.w_dtype = a->w_dtype;
+  cp.out_dtype = a->out_dtype;
+  cp.nsplit = ns;
+  cp.rv_max = vp.rv_max;
+  combine_kernel<<<dim3(lay->num_q_heads, lay->batch), 128, 0, st>>>(cp);
+  rc = fail_launch();
+  if (!rc && ev) cudaEventRecord(ev[3], st);
+  return rc;
+}
+
+int starkv_k_logits(const starkv_layout* lay, const starkv_decode_args* a, float* logits, starkv_stream_t stream) {
+  KParams kp;
+  KGeom g;
+  int rc = prepare_k(lay, a, kp, g);
+  if (rc) return rc;
+  if (!logits || !a->rope_table) return set_error(STARKV_ERR_INVALID, "logits and rope_table are required");
+  const int T = a->num_tokens;
+  const int ns = a->num_splits > 0 ? a->num_splits : auto_splits(*lay, T, device_sm_count(nullptr));
+  const int ntiles = (T + 127) / 128;
+  kp.rope = reinterpret_cast<const float2*>(a->rope_table);
+  kp.logits = logits;
+  kp.nsplit = ns;
+  kp.tps = ((ntiles + ns - 1) / ns) * 128;
+  kp.out_scale = 1.0f;
+  kp.mask_scale = 1.0f;
+  return dispatch_k(kp, g, (cudaStream_t)stream);
+}
+
+int starkv_v_latent(const starkv_layout* lay, const float* probs, int32_t num_tokens, const void* v_cache,
+                    const void* v_params, float* out, starkv_stream_t stream) {
+  int rc = validate(lay);
+  if (rc) return rc;
+  if (!probs || !v_cache || !out || num_tokens <= 0 || num_tokens > lay->capacity ||
+      (lay->quantized && !v_params))
+    return set_error(STARKV_ERR_INVALID, "bad arguments");
+  rc = check_device();
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t n = (size_t)lay->batch * lay->num_q_heads * lay->v_rank_total * sizeof(float);
+  if (cudaMemsetAsync(out, 0, n, st) != cudaSuccess) return fail_launch();
+  VParams vp;
+  memset(&vp, 0, sizeof(vp));
+  vp.lay = *lay;
+  vp.probs = probs;
+  vp.v_cache = v_cache;
+  vp.v_params = reinterpret_cast<const __half2*>(v_params);
+  vp.partial = out;
+  vp.T = num_tokens;
+  vp.nsplit = 1;
+  vp.nsplit_k = 1;
+  vp.tps = num_tokens;
+  vp.rv_max = max_v_rank(*lay);
+  return dispatch_v(vp, 1, st);
+}
+
+int starkv_read_device_error(void* workspace, int* out_code, starkv_stream_t stream) {
+  if (!workspace || !out_code) return set_error(STARKV_ERR_INVALID, "bad arguments");
+  cudaStream_t st = (cudaStream_t)stream;
+  int code = 0;
+  if (cudaMemcpyAsync(&code, workspace, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess) return fail_launch();
+  if (cudaStreamSynchronize(st) != cudaSuccess) return fail_launch();
+  *out_code = code;
+  if (code && cudaMemsetAsync(workspace, 0, sizeof(int), st) != cudaSuccess) return fail_launch();
+  return STARKV_OK;
+}
+
+}  // extern "C"

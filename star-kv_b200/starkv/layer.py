@@ -1,0 +1,74 @@
+"""One compressed-KV attention layer's decode state on the GPU.
+
+``DecodeLayer`` owns the latent cache, the packed K/V up-projections, the RoPE
+table and the workspace of one layer, and runs the step the reference runs in
+``LlamaCustomAttention.forward`` between the latent projections and ``o_proj``
+(LlamaLoRaAttention_headwise.py:98-133, LlamaLoRaAttention_headwise_quant.py:107-186):
+
+    append(new K/V latents)  ->  decode_attention(q_rot)  ->  (B, Hq, 128)
+"""
+
+from __future__ import annotations
+
+from typing import Optional, Sequence
+
+import torch
+
+from . import ops
+
+
+def rope_inv_freq(theta: float, head_dim: int = 128, device=None) -> torch.Tensor:
+    """HF default-rope inverse frequencies, computed with the same torch ops as
+    ``LlamaRotaryEmbedding`` so the fp32 values are identical."""
+    base = float(theta)
+    inv = 1.0 / (base ** (torch.arange(0, head_dim, 2, dtype=torch.int64).to(dtype=torch.float) / head_dim))
+    return inv.to(device=device, dtype=torch.float32).contiguous()
+
+
+class DecodeLayer:
+    def __init__(self, layout, k_u: torch.Tensor, v_u: torch.Tensor, theta: float,
+                 rope: Optional[ops.RopeTable] = None, device=None):
+        """k_u: packed K up-projections (sum_h 128*r_h elements, head h = (128, r_h));
+        v_u: v_proj.U.weight (Hkv*128, R)."""
+        self.layout = layout
+        self.device = torch.device(device or k_u.device)
+        self.cache = ops.LatentCache(layout, self.device)
+        self.k_u = k_u.contiguous()
+        self.v_u = v_u.contiguous()
+        self.scaling = 128 ** -0.5
+        if rope is None:
+            rope = ops.RopeTable(rope_inv_freq(theta, 128, self.device), layout.capacity)
+        self.rope = rope
+        self.num_splits = 0
+
+    @property
+    def length(self) -> int:
+        return self.cache.length
+
+    def prefill(self, k_lat: torch.Tensor, v_lat: torch.Tensor):
+        self.cache.prefill(k_lat.contiguous(), v_lat.contiguous())
+
+    def append(self, k_lat: torch.Tensor, v_lat: torch.Tensor):
+        self.cache.append(k_lat.contiguous(), v_lat.contiguous())
+
+    def attend(self, q_rot: torch.Tensor, mask: Optional[torch.Tensor] = None,
+               out: Optional[torch.Tensor] = None, events=None) -> torch.Tensor:
+        """Attention of the (B, Hq, 128) rotated query over every filled slot."""
+        T = self.cache.length
+        table = self.rope.ensure(T)
+        return ops.decode_attention(self.layout, self.cache, q_rot.contiguous(), self.k_u, self.v_u,
+                                    self.rope.inv_freq, self.scaling, T, rope_table=table,
+                                    mask=None if mask is None else mask.contiguous(), out=out,
+                                    num_splits=self.num_splits, events=events)
+
+    def step(self, q_rot: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+             mask: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+             events=None) -> torch.Tensor:
+        """Append the new token's latents (B, 1, sum r_h) / (B, 1, R), then attend."""
+        self.append(k_new, v_new)
+        return self.attend(q_rot, mask=mask, out=out, events=events)
+
+
+def pack_k_u(k_u_heads: Sequence[torch.Tensor]) -> torch.Tensor:
+    """Concatenate per-head (128, r_h) K up-projections into the packed layout."""
+    return torch.cat([u.contiguous().reshape(-1) for u in k_u_heads])

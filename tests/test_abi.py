@@ -1,0 +1,58 @@
+"""libstarkv.so loads on a CPU-only machine, exports exactly what include/starkv.h
+declares, and validates layouts on the host (no CUDA calls)."""
+
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from starkv import _lib
+
+
+def header_functions():
+    src = open(os.path.join(ROOT, "include", "starkv.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return set(re.findall(r"\b(starkv_\w+)\s*\(", src))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = header_functions()
+    bound = {name for name, _, _ in _lib.SIGNATURES}
+    assert declared == bound, declared ^ bound
+    for name in declared:
+        assert hasattr(lib, name), name
+
+
+def test_layout_abi_size():
+    lib = _lib.load()
+    assert lib.starkv_layout_size() == C.sizeof(_lib.Layout)
+
+
+def test_layout_validation_host_only():
+    import torch
+    from starkv import ops
+    lay = ops.make_layout(2, 8, 8, [16, 32, 96, 48, 16, 16, 64, 80], [64, 192], [4, 4], 300, True, torch.float16)
+    assert lay.k_rank_total == 368 and lay.v_rank_total == 256
+    lib = _lib.load()
+    bad = ops.make_layout(2, 8, 8, [16] * 8, [64, 64], [4, 4], 10, True, torch.float16)
+    bad.k_rank[0] = 24                                               # not a multiple of 16
+    assert lib.starkv_validate_layout(C.byref(bad)) == 2
+    bad.k_rank[0] = 16
+    bad.v_num_kv[1] = 3                                              # blocks do not cover the heads
+    assert lib.starkv_validate_layout(C.byref(bad)) == 1
+    with pytest.raises(_lib.StarKVError):
+        ops.make_layout(2, 8, 8, [256] * 8, [64, 64], [4, 4], 10, True, torch.float16)
+    with pytest.raises(_lib.StarKVError):                            # 16 q heads in one V block
+        ops.make_layout(1, 32, 8, [32] * 8, [64] * 2, [4, 4], 10, True, torch.float16)
+
+
+def test_no_cpu_path():
+    """The ops refuse CPU tensors instead of computing on the host."""
+    import torch
+    from starkv import ops
+    lay = ops.make_layout(1, 4, 4, [16] * 4, [64], [4], 8, True, torch.float16)
+    with pytest.raises(_lib.StarKVError):
+        ops._ptr(torch.zeros(4))

@@ -1,0 +1,132 @@
+"""Decode attention on the B200 against the reference (golden vectors made by the
+reference's own eager module) and the CPU oracle, through the C ABI.
+
+Tolerance (north star): rel-L2 <= 2e-3 and max-abs <= 1e-2 against the fp32 reference."""
+
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import starkv_oracle as O
+from starkv import ops
+from starkv.harness import build_step, device_layer
+from starkv.synthetic import make_layer, make_spec
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+REL_L2, MAX_ABS = 2e-3, 1e-2
+MANIFEST = json.load(open(os.path.join(GOLDEN, "manifest.json")))
+
+
+def _run(data, cuda, num_splits=0):
+    st = build_step(data, cuda)
+    st.layer.num_splits = num_splits
+    out = st.layer.step(st.q, st.k_new, st.v_new, mask=st.mask)
+    torch.cuda.synchronize()
+    assert ops.read_device_error(device=cuda) == 0
+    return out.float().cpu().numpy(), st
+
+
+@pytest.mark.parametrize("name", sorted(MANIFEST))
+def test_decode_matches_reference_golden(cuda, name):
+    m = MANIFEST[name]
+    spec = make_spec(m["config"], seed=0, **m["overrides"])
+    data = make_layer(spec, with_mask=m["with_mask"])
+    out, _ = _run(data, cuda)
+    gold = np.load(os.path.join(GOLDEN, f"{name}.npz"))["attn"].reshape(out.shape)
+    assert O.rel_l2(out, gold) <= REL_L2
+    assert np.abs(out - gold).max() <= MAX_ABS
+
+
+@pytest.mark.parametrize("cfg,over,mask", [
+    ("c1", dict(num_q_heads=8, batch=2, context=127), False),     # T = 128 exactly
+    ("c1", dict(num_q_heads=8, batch=2, context=128), False),     # T = 129 (one-row tail)
+    ("c1", dict(num_q_heads=4, batch=1, context=1), False),       # T = 2
+    ("c1", dict(num_q_heads=32, batch=3, context=1500), True),
+    ("c2", dict(num_q_heads=32, num_kv_heads=8, batch=2, context=2000), False),
+    ("c0", dict(num_q_heads=8, batch=2, context=700, dtype="float16"), False),
+    ("c0", dict(num_q_heads=8, batch=2, context=700, dtype="bfloat16"), True),
+])
+def test_decode_matches_oracle(cuda, cfg, over, mask):
+    spec = make_spec(cfg, seed=11, **over)
+    data = make_layer(spec, with_mask=mask)
+    out, _ = _run(data, cuda)
+    ref = O.layer_reference(data)
+    assert O.rel_l2(out, ref) <= REL_L2
+    assert np.abs(out - ref).max() <= MAX_ABS
+
+
+def test_split_count_invariance_and_determinism(cuda):
+    spec = make_spec("c1", seed=12, num_q_heads=8, batch=2, context=3000)
+    data = make_layer(spec)
+    a, _ = _run(data, cuda, num_splits=1)
+    b, _ = _run(data, cuda, num_splits=7)
+    c, _ = _run(data, cuda, num_splits=7)
+    np.testing.assert_array_equal(b, c)
+    assert O.rel_l2(a, b) < 1e-5
+
+
+def test_k_logits_matches_oracle(cuda):
+    """abx's contract: unscaled q . RoPE(X U^T) per position."""
+    spec = make_spec("c1", seed=13, num_q_heads=8, batch=2, context=900)
+    data = make_layer(spec)
+    st = build_step(data, cuda)
+    st.layer.append(st.k_new, st.v_new)
+    T = spec.tokens
+    table = st.layer.rope.ensure(T)
+    lg = ops.k_logits(st.layer.layout, st.layer.cache, st.q, st.layer.k_u, table, st.layer.rope.inv_freq, T)
+    qz = O.quantize_layer(data.xk, data.xv, spec.context)
+    cos, sin = O.rope_cos_sin(np.arange(T), O.rope_inv_freq(spec.theta))
+    for h in range(spec.num_q_heads):
+        keys = O.apply_rope(qz["xk_hat"][h].astype(np.float64) @ data.k_u[h].astype(np.float64).T, cos, sin)
+        ref = np.einsum("bld,bd->bl", keys, data.q[:, h].astype(np.float64))
+        got = lg[:, h].cpu().numpy()
+        assert O.rel_l2(got, ref) < 2e-3
+
+
+def test_v_latent_matches_oracle(cuda):
+    """bx's contract: P @ dequant(X_v) per head, zero outside the head's V block."""
+    spec = make_spec("c1", seed=14, num_q_heads=8, batch=2, context=700)
+    data = make_layer(spec)
+    st = build_step(data, cuda)
+    st.layer.append(st.k_new, st.v_new)
+    T = spec.tokens
+    rng = np.random.default_rng(0)
+    p = rng.random((spec.batch, spec.num_q_heads, T)).astype(np.float32)
+    p /= p.sum(-1, keepdims=True)
+    got = ops.v_latent(st.layer.layout, st.layer.cache, torch.from_numpy(p).to(cuda), T).cpu().numpy()
+    xv = O.quantize_layer(data.xk, data.xv, spec.context)["xv_hat"]
+    vb = spec.v_block_of_kv()
+    vcol = np.concatenate([[0], np.cumsum(spec.v_ranks)])
+    for h in range(spec.num_q_heads):
+        j = vb[h]
+        ref = np.zeros((spec.batch, spec.v_rank_total))
+        ref[:, vcol[j]:vcol[j + 1]] = np.einsum("bl,blr->br", p[:, h], xv[:, :, vcol[j]:vcol[j + 1]])
+        assert O.rel_l2(got[:, h], ref) < 1e-5
+
+
+def test_full_size_c1_sequence0_against_oracle(cuda):
+    """BASELINE config 1 at full size (B=16, 32K context, 32 heads): sequence 0 and
+    15 against the oracle, all sequences finite, and the device error word clear."""
+    spec = make_spec("c1")
+    st, k_u_heads, v_u = device_layer(spec, cuda, seed=1)
+    out = st.layer.step(st.q, st.k_new, st.v_new).float()
+    torch.cuda.synchronize()
+    assert ops.read_device_error(device=cuda) == 0
+    assert torch.isfinite(out).all()
+    for b in (0, spec.batch - 1):
+        xk = [st.k_lat[b:b + 1, :, c0:c0 + r].float().cpu().numpy()
+              for c0, r in zip(np.concatenate([[0], np.cumsum(spec.k_ranks)[:-1]]), spec.k_ranks)]
+        xv = st.v_lat[b:b + 1].float().cpu().numpy()
+        qz = O.quantize_layer(xk, xv, spec.context)
+        ref = O.decode_attention(st.q[b:b + 1].float().cpu().numpy(), qz["xk_hat"],
+                                 [u.float().cpu().numpy() for u in k_u_heads], qz["xv_hat"],
+                                 v_u.float().cpu().numpy(), spec.k_ranks, spec.v_ranks, spec.v_block_of_kv(),
+                                 O.rope_inv_freq(spec.theta), 128 ** -0.5, dtype=np.float32)
+        got = out[b:b + 1].cpu().numpy()
+        assert O.rel_l2(got, ref) <= REL_L2
+        assert np.abs(got - ref).max() <= MAX_ABS
