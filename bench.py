@@ -251,6 +251,8 @@ def main():
     K = args.steps
     kev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for e in [x for row in kev for x in row] + [t0, t1]:
+        e.record()                                  # create the CUDA events before the timed region
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()

@@ -140,9 +140,6 @@ typedef struct starkv_decode_args {
   const void* v_params;
   void* out;                /* (B, Hq, 128) out_dtype */
   int32_t out_dtype;
-  const void* rope_table;   /* optional (>= num_tokens, 64) fp32 (cos, sin) pairs of fl(l * inv_freq[i]),
-                               kept by the caller across steps/layers (starkv_rope_table); NULL: the
-                               call computes it into its workspace */
   int32_t num_splits;       /* sequence splits per (sequence, head group); 0 = automatic */
   void* workspace;          /* scratch, 256-byte aligned */
   size_t workspace_bytes;
@@ -184,17 +181,16 @@ int starkv_v_latent(const starkv_layout* lay, const float* probs, int32_t num_to
                     const void* v_cache, const void* v_params, float* out, starkv_stream_t stream);
 
 /*
- * Fill rows [first, first + count) of a RoPE table (fp32 (cos, sin) pairs,
- * 64 per row): table[l][i] = (cos, sin)(fl(l * inv_freq[i])), the angles of the
- * HF LlamaRotaryEmbedding tables the reference applies at
- * LlamaLoRaAttention_headwise.py:109.  Rows depend only on the position, so one
- * table serves every layer and grows by one row per decode step.
+ * Diagnostics: when `buffer` is non-NULL, later K-path launches record a
+ * per-job clock64 timeline (10 int64 fields per job, `jobs` jobs) of the CTAs
+ * (split 0, head group 0, sequence 0 and 1) into it: converter begin / codes
+ * landed / A buffer free / converted / A published, MMA issue, drain wait /
+ * accumulator ready / drain done.  NULL turns it off.  Not for production use.
  */
-int starkv_rope_table(const float* inv_freq, int32_t first, int32_t count, void* table,
-                      starkv_stream_t stream);
+int starkv_debug_trace(void* buffer, int32_t jobs);
 
 /* Reads and clears the device error word at the start of a decode workspace
- * (host pointer `out_code`; synchronises the stream).  0 = no device-side error. */
+ * (synchronises the stream); *out_code = 0 means no device-side error. */
 int starkv_read_device_error(void* workspace, int* out_code, starkv_stream_t stream);
 
 /* Last CUDA error string seen by the library on this thread (for diagnostics). */

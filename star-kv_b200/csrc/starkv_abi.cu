@@ -18,6 +18,8 @@ using namespace starkv;
 namespace {
 
 thread_local char g_last_error[256] = "";
+long long* g_trace = nullptr;  // starkv_debug_trace
+int g_trace_jobs = 0;
 
 int fail_launch() {
   const cudaError_t e = cudaGetLastError();
@@ -76,9 +78,10 @@ int max_v_rank(const starkv_layout& l) {
 }
 int k_elem_bytes(const starkv_layout& l) { return l.quantized ? 1 : dtype_bytes(l.latent_dtype); }
 
-// K-path geometry: heads per CTA (G) and staging stages (S) that fit shared memory.
+// K-path geometry: heads per CTA (G) and the shared memory that fits (one CTA
+// per SM: it owns all 512 TMEM columns).
 struct KGeom {
-  int G, S, rmax;
+  int G, rmax, bsum;
   size_t smem;
 };
 
@@ -86,23 +89,27 @@ KGeom k_geometry(const starkv_layout& l) {
   KGeom g;
   g.rmax = max_k_rank(l);
   const int xb = k_elem_bytes(l);
-  const int Hq = l.num_q_heads;
+  const int Hq = l.num_q_heads, qpk = l.num_q_heads / l.num_kv_heads;
   for (int G = 4; G >= 1; G >>= 1) {
     if (Hq % G) continue;
-    for (int S = 4; S >= 2; --S) {
-      const size_t bytes = k_smem_bytes(G, S, g.rmax, xb);
-      if (bytes <= 227 * 1024) {
-        g.G = G;
-        g.S = S;
-        // at least 80 KB so that no more than two CTAs (2 x 256 TMEM columns) share an SM
-        g.smem = bytes < 80 * 1024 ? 80 * 1024 : bytes;
-        return g;
-      }
+    int bsum = 0;
+    for (int grp = 0; grp < Hq / G; ++grp) {
+      int s = 0;
+      for (int k = 0; k < G; ++k) s += l.k_rank[(grp * G + k) / qpk];
+      bsum = s > bsum ? s : bsum;
+    }
+    const size_t bytes = k_smem_bytes(bsum, g.rmax, xb);
+    if (bytes <= 227 * 1024) {
+      g.G = G;
+      g.bsum = bsum;
+      g.smem = bytes < 116 * 1024 ? 116 * 1024 : bytes;  // never two CTAs (2 x 512 TMEM columns) per SM
+      return g;
     }
   }
   g.G = 0;
-  g.S = 0;
+  g.bsum = 0;
   g.smem = 0;
+  g.rmax = 0;
   return g;
 }
 
@@ -111,8 +118,7 @@ int auto_splits(const starkv_layout& l, int T, int sms) {
   if (g.G == 0 || T <= 0) return 1;
   const int ntiles = (T + 127) / 128;
   const long base = (long)l.batch * (l.num_q_heads / g.G);
-  const int per_sm = g.smem > 113 * 1024 ? 1 : 2;
-  const long slots = (long)(sms > 0 ? sms : 148) * per_sm;
+  const long slots = (long)(sms > 0 ? sms : 148);
   int best = 1;
   double best_t = 1e30;
   for (int ns = 1; ns <= ntiles && ns <= 128; ++ns) {
@@ -129,7 +135,7 @@ int auto_splits(const starkv_layout& l, int T, int sms) {
 }
 
 struct WsLayout {
-  size_t err, logits, stats, partial, rope, total;
+  size_t err, logits, stats, partial, total;
 };
 
 WsLayout ws_layout(const starkv_layout& l, int T, int ns) {
@@ -139,8 +145,7 @@ WsLayout ws_layout(const starkv_layout& l, int T, int ns) {
   w.logits = 256;
   w.stats = w.logits + align256(BH * T * sizeof(float));
   w.partial = w.stats + align256(BH * ns * sizeof(float2));
-  w.rope = w.partial + align256(BH * ns * max_v_rank(l) * sizeof(float));
-  w.total = w.rope + align256((size_t)T * 64 * sizeof(float2));
+  w.total = w.partial + align256(BH * ns * max_v_rank(l) * sizeof(float));
   return w;
 }
 
@@ -242,13 +247,6 @@ int dispatch_v(const VParams& vp, int nsplit, cudaStream_t st) {
   }
 }
 
-int launch_rope(const float* inv_freq, int first, int count, float2* table, cudaStream_t st) {
-  if (count <= 0) return STARKV_OK;
-  const int64_t n = (int64_t)count * 64;
-  rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(inv_freq, first, count, table);
-  return fail_launch();
-}
-
 // Shared front half of decode / logits: validation + K-path parameters.
 int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp, KGeom& g) {
   int rc = validate(lay);
@@ -270,8 +268,11 @@ int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp
   kp.w_dtype = a->w_dtype;
   kp.T = a->num_tokens;
   kp.G = g.G;
-  kp.S = g.S;
   kp.rmax = g.rmax;
+  kp.bsum = g.bsum;
+  kp.inv_freq = a->inv_freq;
+  kp.trace = g_trace;
+  kp.trace_jobs = g_trace_jobs;
   return STARKV_OK;
 }
 
@@ -298,13 +299,6 @@ int starkv_decode_workspace_size(const starkv_layout* lay, int32_t num_tokens, i
   const int ns = num_splits > 0 ? num_splits : starkv_auto_splits(lay, num_tokens);
   *bytes = ws_layout(*lay, num_tokens, ns).total;
   return STARKV_OK;
-}
-
-int starkv_rope_table(const float* inv_freq, int32_t first, int32_t count, void* table, starkv_stream_t stream) {
-  if (!inv_freq || !table || first < 0 || count < 0) return set_error(STARKV_ERR_INVALID, "bad arguments");
-  int rc = check_device();
-  if (rc) return rc;
-  return launch_rope(inv_freq, first, count, reinterpret_cast<float2*>(table), (cudaStream_t)stream);
 }
 
 int starkv_quantize_prefill(const starkv_layout* lay, const void* k_lat, const void* v_lat, int32_t num_tokens,
@@ -410,15 +404,8 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   cudaStream_t st = (cudaStream_t)stream;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
 
-  const float2* rope = reinterpret_cast<const float2*>(a->rope_table);
-  if (!rope) {
-    rc = launch_rope(a->inv_freq, 0, T, reinterpret_cast<float2*>(ws + w.rope), st);
-    if (rc) return rc;
-    rope = reinterpret_cast<const float2*>(ws + w.rope);
-  }
   const int ntiles = (T + 127) / 128;
   const int tiles_per = (ntiles + ns - 1) / ns;
-  kp.rope = rope;
   kp.mask = a->mask;
   kp.logits = reinterpret_cast<float*>(ws + w.logits);
   kp.stats = reinterpret_cast<float2*>(ws + w.stats);
@@ -472,11 +459,10 @@ int starkv_k_logits(const starkv_layout* lay, const starkv_decode_args* a, float
   KGeom g;
   int rc = prepare_k(lay, a, kp, g);
   if (rc) return rc;
-  if (!logits || !a->rope_table) return set_error(STARKV_ERR_INVALID, "logits and rope_table are required");
+  if (!logits) return set_error(STARKV_ERR_INVALID, "logits is required");
   const int T = a->num_tokens;
   const int ns = a->num_splits > 0 ? a->num_splits : auto_splits(*lay, T, device_sm_count(nullptr));
   const int ntiles = (T + 127) / 128;
-  kp.rope = reinterpret_cast<const float2*>(a->rope_table);
   kp.logits = logits;
   kp.nsplit = ns;
   kp.tps = ((ntiles + ns - 1) / ns) * 128;
@@ -510,6 +496,12 @@ int starkv_v_latent(const starkv_layout* lay, const float* probs, int32_t num_to
   vp.tps = num_tokens;
   vp.rv_max = max_v_rank(*lay);
   return dispatch_v(vp, 1, st);
+}
+
+int starkv_debug_trace(void* buffer, int32_t jobs) {
+  g_trace = reinterpret_cast<long long*>(buffer);
+  g_trace_jobs = buffer ? jobs : 0;
+  return STARKV_OK;
 }
 
 int starkv_read_device_error(void* workspace, int* out_code, starkv_stream_t stream) {

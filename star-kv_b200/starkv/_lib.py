@@ -44,7 +44,7 @@ class DecodeArgs(C.Structure):
         ("scaling", C.c_float), ("num_tokens", C.c_int32),
         ("k_cache", C.c_void_p), ("k_scales", C.c_void_p), ("v_cache", C.c_void_p), ("v_params", C.c_void_p),
         ("out", C.c_void_p), ("out_dtype", C.c_int32),
-        ("rope_table", C.c_void_p), ("num_splits", C.c_int32),
+        ("num_splits", C.c_int32),
         ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
         ("events", C.POINTER(C.c_void_p)),
     ]
@@ -64,7 +64,7 @@ SIGNATURES = [
     ("starkv_k_logits", C.c_int, [C.POINTER(Layout), C.POINTER(DecodeArgs), C.c_void_p, C.c_void_p]),
     ("starkv_v_latent", C.c_int, [C.POINTER(Layout), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_void_p]),
-    ("starkv_rope_table", C.c_int, [C.c_void_p, C.c_int32, C.c_int32, C.c_void_p, C.c_void_p]),
+    ("starkv_debug_trace", C.c_int, [C.c_void_p, C.c_int32]),
     ("starkv_read_device_error", C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.c_void_p]),
     ("starkv_last_error", C.c_char_p, []),
 ]

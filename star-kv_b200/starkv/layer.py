@@ -27,7 +27,7 @@ def rope_inv_freq(theta: float, head_dim: int = 128, device=None) -> torch.Tenso
 
 class DecodeLayer:
     def __init__(self, layout, k_u: torch.Tensor, v_u: torch.Tensor, theta: float,
-                 rope: Optional[ops.RopeTable] = None, device=None):
+                 device=None):
         """k_u: packed K up-projections (sum_h 128*r_h elements, head h = (128, r_h));
         v_u: v_proj.U.weight (Hkv*128, R)."""
         self.layout = layout
@@ -36,9 +36,7 @@ class DecodeLayer:
         self.k_u = k_u.contiguous()
         self.v_u = v_u.contiguous()
         self.scaling = 128 ** -0.5
-        if rope is None:
-            rope = ops.RopeTable(rope_inv_freq(theta, 128, self.device), layout.capacity)
-        self.rope = rope
+        self.inv_freq = rope_inv_freq(theta, 128, self.device)
         self.num_splits = 0
 
     @property
@@ -55,10 +53,8 @@ class DecodeLayer:
                out: Optional[torch.Tensor] = None, events=None) -> torch.Tensor:
         """Attention of the (B, Hq, 128) rotated query over every filled slot."""
         T = self.cache.length
-        table = self.rope.ensure(T)
         return ops.decode_attention(self.layout, self.cache, q_rot.contiguous(), self.k_u, self.v_u,
-                                    self.rope.inv_freq, self.scaling, T, rope_table=table,
-                                    mask=None if mask is None else mask.contiguous(), out=out,
+                                    self.inv_freq, self.scaling, T, mask=None if mask is None else mask.contiguous(), out=out,
                                     num_splits=self.num_splits, events=events)
 
     def step(self, q_rot: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,

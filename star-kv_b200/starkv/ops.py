@@ -155,26 +155,6 @@ class LatentCache:
         return self.k_cache[L.k_offset[h]:L.k_offset[h] + n].view(L.batch, L.capacity, r)
 
 
-class RopeTable:
-    """fp32 (cos, sin) table of fl(l * inv_freq_i), rows 0..capacity-1, filled on
-    demand; shared by every layer with the same inv_freq."""
-
-    def __init__(self, inv_freq: torch.Tensor, capacity: int):
-        _require(inv_freq, "inv_freq", torch.float32, 64, align=4)
-        self.inv_freq = inv_freq
-        self.table = torch.empty(capacity, 64, 2, dtype=torch.float32, device=inv_freq.device)
-        self.rows = 0
-
-    def ensure(self, n: int) -> torch.Tensor:
-        if n > self.table.shape[0]:
-            raise _lib.StarKVError("rope table capacity exceeded")
-        if n > self.rows:
-            check(load().starkv_rope_table(_ptr(self.inv_freq), self.rows, n - self.rows, _ptr(self.table),
-                                           _stream()), "starkv_rope_table")
-            self.rows = n
-        return self.table
-
-
 _WORKSPACES = {}
 
 
@@ -197,8 +177,7 @@ def workspace_size(layout: Layout, num_tokens: int, num_splits: int = 0) -> int:
     return int(n.value)
 
 
-def _decode_args(layout, cache, q, k_u, v_u, inv_freq, scaling, num_tokens, rope_table, mask, out,
-                 ws, num_splits):
+def _decode_args(layout, cache, q, k_u, v_u, inv_freq, scaling, num_tokens, mask, out, ws, num_splits):
     a = DecodeArgs()
     a.q, a.q_dtype = _ptr(q), dtype_code(q.dtype)
     a.w_dtype = dtype_code(k_u.dtype)
@@ -211,7 +190,6 @@ def _decode_args(layout, cache, q, k_u, v_u, inv_freq, scaling, num_tokens, rope
     a.v_cache, a.v_params = _ptr(cache.v_cache), _ptr(cache.v_params)
     a.out = _ptr(out)
     a.out_dtype = dtype_code(out.dtype) if out is not None else 0
-    a.rope_table = _ptr(rope_table)
     a.num_splits = int(num_splits)
     a.workspace = _ptr(ws)
     a.workspace_bytes = ws.numel() if ws is not None else 0
@@ -220,7 +198,7 @@ def _decode_args(layout, cache, q, k_u, v_u, inv_freq, scaling, num_tokens, rope
 
 def decode_attention(layout: Layout, cache: LatentCache, q: torch.Tensor, k_u: torch.Tensor,
                      v_u: torch.Tensor, inv_freq: torch.Tensor, scaling: float, num_tokens: Optional[int] = None,
-                     rope_table: Optional[torch.Tensor] = None, mask: Optional[torch.Tensor] = None,
+                     mask: Optional[torch.Tensor] = None,
                      out: Optional[torch.Tensor] = None, num_splits: int = 0,
                      ws: Optional[torch.Tensor] = None, events=None) -> torch.Tensor:
     """One decode step of compressed-KV attention over cache slots [0, num_tokens).
@@ -239,8 +217,13 @@ def decode_attention(layout: Layout, cache: LatentCache, q: torch.Tensor, k_u: t
         out = torch.empty(B, Hq, 128, dtype=q.dtype, device=q.device)
     if ws is None:
         ws = workspace(workspace_size(layout, T, num_splits), q.device)
-    a = _decode_args(layout, cache, q, k_u, v_u, inv_freq, scaling, T, rope_table, mask, out, ws, num_splits)
+    _require(inv_freq, "inv_freq", torch.float32, 64, align=4)
+    a = _decode_args(layout, cache, q, k_u, v_u, inv_freq, scaling, T, mask, out, ws, num_splits)
     if events is not None:
+        # torch creates CUDA events lazily: record each once to obtain its handle
+        for e in events:
+            if not e.cuda_event:
+                e.record()
         # four torch.cuda.Event(enable_timing=True): before K, after K, after V, after the merge
         arr = (C.c_void_p * 4)(*[C.c_void_p(e.cuda_event) for e in events])
         a.events = C.cast(arr, C.POINTER(C.c_void_p))
@@ -248,13 +231,13 @@ def decode_attention(layout: Layout, cache: LatentCache, q: torch.Tensor, k_u: t
     return out
 
 
-def k_logits(layout: Layout, cache: LatentCache, q: torch.Tensor, k_u: torch.Tensor, rope_table: torch.Tensor,
-             inv_freq: torch.Tensor, num_tokens: int, num_splits: int = 0) -> torch.Tensor:
+def k_logits(layout: Layout, cache: LatentCache, q: torch.Tensor, k_u: torch.Tensor, inv_freq: torch.Tensor,
+             num_tokens: int, num_splits: int = 0) -> torch.Tensor:
     """logits[b, qh, l] = q . RoPE_l(X_k @ U^T), unscaled fp32 (B, Hq, num_tokens) — abx's contract."""
     B, Hq = layout.batch, layout.num_q_heads
     logits = torch.empty(B, Hq, num_tokens, dtype=torch.float32, device=q.device)
-    a = _decode_args(layout, cache, q, k_u, None, inv_freq, 1.0, num_tokens, rope_table, None, None, None,
-                     num_splits)
+    _require(inv_freq, "inv_freq", torch.float32, 64, align=4)
+    a = _decode_args(layout, cache, q, k_u, None, inv_freq, 1.0, num_tokens, None, None, None, num_splits)
     check(load().starkv_k_logits(C.byref(layout), C.byref(a), _ptr(logits), _stream()), "starkv_k_logits")
     return logits
 

@@ -67,7 +67,7 @@ def test_split_count_invariance_and_determinism(cuda):
     b, _ = _run(data, cuda, num_splits=7)
     c, _ = _run(data, cuda, num_splits=7)
     np.testing.assert_array_equal(b, c)
-    assert O.rel_l2(a, b) < 1e-5
+    assert O.rel_l2(a, b) < 2e-4            # outputs are fp16: split order only moves the last bit
 
 
 def test_k_logits_matches_oracle(cuda):
@@ -77,8 +77,7 @@ def test_k_logits_matches_oracle(cuda):
     st = build_step(data, cuda)
     st.layer.append(st.k_new, st.v_new)
     T = spec.tokens
-    table = st.layer.rope.ensure(T)
-    lg = ops.k_logits(st.layer.layout, st.layer.cache, st.q, st.layer.k_u, table, st.layer.rope.inv_freq, T)
+    lg = ops.k_logits(st.layer.layout, st.layer.cache, st.q, st.layer.k_u, st.layer.inv_freq, T)
     qz = O.quantize_layer(data.xk, data.xv, spec.context)
     cos, sin = O.rope_cos_sin(np.arange(T), O.rope_inv_freq(spec.theta))
     for h in range(spec.num_q_heads):

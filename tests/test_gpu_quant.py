@@ -46,7 +46,7 @@ def test_prefill_and_append_bit_exact(cuda, cfg, over):
 def test_append_saturates_and_handles_constant_groups(cuda):
     spec = make_spec("c1", seed=5, num_q_heads=4, batch=2, context=64)
     data = make_layer(spec)
-    data.xk[0][:, -1, :] *= 50.0                     # far beyond the prefill range
+    data.xk[0][:, -1, :] = (data.xk[0][:, -1, :] * 50.0).astype(np.float16).astype(np.float32)  # beyond the prefill range
     data.xv[:, -1, :32] = 0.25                       # constant group
     st = build_step(data, cuda)
     st.layer.append(st.k_new, st.v_new)
