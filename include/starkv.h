@@ -181,6 +181,26 @@ int starkv_v_latent(const starkv_layout* lay, const float* probs, int32_t num_to
                     const void* v_cache, const void* v_params, float* out, starkv_stream_t stream);
 
 /*
+ * starkv_decode_attention for callers that cannot allocate device memory when
+ * they run a decode step (plugins that receive only input/output buffers, code
+ * running under another framework's memory pool or a locked-down allocator).
+ * No counterpart in the reference.  The scratch of the step lives in a fixed
+ * static device array of starkv_static_scratch_bytes() bytes (32 MiB) that
+ * every GPU loading the library reserves until the process exits; args->
+ * workspace and workspace_bytes are ignored.  Steps whose scratch would exceed
+ * it (starkv_decode_workspace_size) are rejected with STARKV_ERR_WORKSPACE.
+ * The first call on a device looks up the array's device address with that
+ * device current, so make it before any stream capture.  All calls share the
+ * one array: calls that can overlap on the GPU (other streams, other threads)
+ * race and must be serialised by the caller.  Allocates nothing.
+ */
+int starkv_decode_attention_static(const starkv_layout* lay, const starkv_decode_args* args,
+                                   starkv_stream_t stream);
+
+/* Size in bytes of the static scratch used by starkv_decode_attention_static. */
+size_t starkv_static_scratch_bytes(void);
+
+/*
  * Diagnostics: when `buffer` is non-NULL, later K-path launches record a
  * per-job clock64 timeline (10 int64 fields per job, `jobs` jobs) of the CTAs
  * (split 0, head group 0, sequence 0 and 1) into it: converter begin / codes

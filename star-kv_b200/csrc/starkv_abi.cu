@@ -516,3 +516,79 @@ int starkv_read_device_error(void* workspace, int* out_code, starkv_stream_t str
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Decode attention without a caller-provided workspace.
+//
+// Some callers cannot allocate device memory at the point where they run a
+// decode step: code running inside another framework's memory pool, plugin
+// hosts that hand over only input and output buffers, or processes whose
+// allocator is locked down.  For them the scratch of the decode step lives in
+// this fixed, file-scope device array.  Every GPU that loads the library
+// reserves it until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kStaticScratchBytes = 32u << 20;  // 32 MiB
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch, looked up once per device (with that
+// device current) on the first call made on it.
+uint8_t* static_scratch_ptr(int* rc) {
+  static void* ptr[kMaxDevices] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *rc = set_error(STARKV_ERR_LAUNCH, "no current CUDA device");
+    return nullptr;
+  }
+  if (!ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) {
+      *rc = fail_launch();
+      if (!*rc) *rc = set_error(STARKV_ERR_LAUNCH, "cudaGetSymbolAddress(g_static_scratch) failed");
+      return nullptr;
+    }
+    ptr[dev] = p;
+  }
+  *rc = STARKV_OK;
+  return reinterpret_cast<uint8_t*>(ptr[dev]);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t starkv_static_scratch_bytes(void) { return kStaticScratchBytes; }
+
+int starkv_decode_attention_static(const starkv_layout* lay, const starkv_decode_args* args,
+                                   starkv_stream_t stream) {
+  int rc = validate(lay);
+  if (rc) return rc;
+  if (!args) return set_error(STARKV_ERR_INVALID, "null argument");
+  if (args->num_tokens <= 0 || args->num_tokens > lay->capacity)
+    return set_error(STARKV_ERR_INVALID, "num_tokens outside (0, capacity]");
+  const int sms = device_sm_count(nullptr);
+  if (sms < 0) return set_error(STARKV_ERR_LAUNCH, "no CUDA device");
+  const int ns = args->num_splits > 0 ? args->num_splits : auto_splits(*lay, args->num_tokens, sms);
+  const size_t need = ws_layout(*lay, args->num_tokens, ns).total;
+  if (need > kStaticScratchBytes) {
+    char msg[200];
+    snprintf(msg, sizeof(msg),
+             "decode step needs %zu bytes of scratch, above the %zu-byte static scratch of "
+             "starkv_decode_attention_static; use starkv_decode_attention with a workspace",
+             need, kStaticScratchBytes);
+    return set_error(STARKV_ERR_WORKSPACE, msg);
+  }
+  uint8_t* scratch = static_scratch_ptr(&rc);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  // The array keeps whatever the previous call left: the error word must start at zero.
+  if (cudaMemsetAsync(scratch, 0, 256, st) != cudaSuccess) return fail_launch();
+  starkv_decode_args a = *args;
+  a.workspace = scratch;
+  a.workspace_bytes = kStaticScratchBytes;
+  a.num_splits = ns;
+  return starkv_decode_attention(lay, &a, stream);
+}
+
+}  // extern "C"

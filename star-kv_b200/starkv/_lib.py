@@ -65,6 +65,8 @@ SIGNATURES = [
     ("starkv_v_latent", C.c_int, [C.POINTER(Layout), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_void_p]),
     ("starkv_debug_trace", C.c_int, [C.c_void_p, C.c_int32]),
+    ("starkv_decode_attention_static", C.c_int, [C.POINTER(Layout), C.POINTER(DecodeArgs), C.c_void_p]),
+    ("starkv_static_scratch_bytes", C.c_size_t, []),
     ("starkv_read_device_error", C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.c_void_p]),
     ("starkv_last_error", C.c_char_p, []),
 ]

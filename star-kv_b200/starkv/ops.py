@@ -231,6 +231,19 @@ def decode_attention(layout: Layout, cache: LatentCache, q: torch.Tensor, k_u: t
     return out
 
 
+def decode_attention_static(layout: Layout, cache: LatentCache, q: torch.Tensor, k_u: torch.Tensor,
+                            v_u: torch.Tensor, inv_freq: torch.Tensor, scaling: float, num_tokens: int,
+                            out: torch.Tensor, mask: Optional[torch.Tensor] = None, num_splits: int = 0) -> torch.Tensor:
+    """``decode_attention`` through ``starkv_decode_attention_static``: for callers that
+    cannot allocate device memory during the step, the library's fixed static scratch
+    replaces the workspace.  ``out`` must be provided (nothing is allocated here)."""
+    _require(inv_freq, "inv_freq", torch.float32, 64, align=4)
+    a = _decode_args(layout, cache, q, k_u, v_u, inv_freq, scaling, num_tokens, mask, out, None, num_splits)
+    check(load().starkv_decode_attention_static(C.byref(layout), C.byref(a), _stream()),
+          "starkv_decode_attention_static")
+    return out
+
+
 def k_logits(layout: Layout, cache: LatentCache, q: torch.Tensor, k_u: torch.Tensor, inv_freq: torch.Tensor,
              num_tokens: int, num_splits: int = 0) -> torch.Tensor:
     """logits[b, qh, l] = q . RoPE_l(X_k @ U^T), unscaled fp32 (B, Hq, num_tokens) — abx's contract."""
