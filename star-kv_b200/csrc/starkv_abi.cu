@@ -53,10 +53,10 @@ int device_sm_count(int* dev_out) {
 // Raise a kernel's dynamic shared-memory limit once per (kernel, device).
 template <typename K>
 int ensure_smem(K kernel, size_t bytes, int slot) {
-  static size_t configured[8][kMaxDevices] = {{0}};
+  static size_t configured[16][kMaxDevices] = {{0}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= kMaxDevices || slot < 0 || slot >= 8) return STARKV_ERR_INVALID;
+  if (dev < 0 || dev >= kMaxDevices || slot < 0 || slot >= 16) return STARKV_ERR_INVALID;
   if (configured[slot][dev] >= bytes) return STARKV_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
     return fail_launch();
@@ -81,7 +81,7 @@ int k_elem_bytes(const starkv_layout& l) { return l.quantized ? 1 : dtype_bytes(
 // K-path geometry: heads per CTA (G) and the shared memory that fits (one CTA
 // per SM: it owns all 512 TMEM columns).
 struct KGeom {
-  int G, rmax, bsum;
+  int G, rmax, bsum, pitch16max;
   size_t smem;
 };
 
@@ -90,6 +90,11 @@ KGeom k_geometry(const starkv_layout& l) {
   g.rmax = max_k_rank(l);
   const int xb = k_elem_bytes(l);
   const int Hq = l.num_q_heads, qpk = l.num_q_heads / l.num_kv_heads;
+  g.pitch16max = 0;
+  for (int h = 0; h < l.num_kv_heads; ++h) {
+    const int pt = k_pitch16(l.k_rank[h], xb);
+    g.pitch16max = pt > g.pitch16max ? pt : g.pitch16max;
+  }
   for (int G = 4; G >= 1; G >>= 1) {
     if (Hq % G) continue;
     int bsum = 0;
@@ -98,7 +103,7 @@ KGeom k_geometry(const starkv_layout& l) {
       for (int k = 0; k < G; ++k) s += l.k_rank[(grp * G + k) / qpk];
       bsum = s > bsum ? s : bsum;
     }
-    const size_t bytes = k_smem_bytes(bsum, g.rmax, xb);
+    const size_t bytes = k_smem_bytes(bsum, g.rmax, g.pitch16max, xb);
     if (bytes <= 227 * 1024) {
       g.G = G;
       g.bsum = bsum;
@@ -206,15 +211,24 @@ inline unsigned grid1d(int64_t n, int threads) {
   return (unsigned)b;
 }
 
-template <typename XT, bool QUANT>
-int launch_k(const KParams& kp, const KGeom& g, cudaStream_t st) {
-  auto kern = k_logits_kernel<XT, QUANT>;
-  const int slot = QUANT ? 0 : (sizeof(XT) == 4 ? 1 : (std::is_same<XT, __half>::value ? 2 : 3));
+template <typename XT, bool QUANT, int G>
+int launch_kg(const KParams& kp, const KGeom& g, cudaStream_t st) {
+  auto kern = k_logits_kernel<XT, QUANT, G>;
+  const int slot = 3 * (QUANT ? 0 : (sizeof(XT) == 4 ? 1 : (std::is_same<XT, __half>::value ? 2 : 3))) + (G == 4 ? 0 : G == 2 ? 1 : 2);
   int rc = ensure_smem(kern, g.smem, slot);
   if (rc) return rc;
   dim3 grid(kp.nsplit, kp.lay.num_q_heads / kp.G, kp.lay.batch);
   kern<<<grid, kKThreads, g.smem, st>>>(kp);
   return fail_launch();
+}
+
+template <typename XT, bool QUANT>
+int launch_k(const KParams& kp, const KGeom& g, cudaStream_t st) {
+  switch (kp.G) {
+    case 4: return launch_kg<XT, QUANT, 4>(kp, g, st);
+    case 2: return launch_kg<XT, QUANT, 2>(kp, g, st);
+    default: return launch_kg<XT, QUANT, 1>(kp, g, st);
+  }
 }
 
 int dispatch_k(const KParams& kp, const KGeom& g, cudaStream_t st) {
@@ -229,8 +243,8 @@ int dispatch_k(const KParams& kp, const KGeom& g, cudaStream_t st) {
 template <typename LT, bool QUANT>
 int launch_v(const VParams& vp, int nsplit, cudaStream_t st) {
   auto kern = v_latent_kernel<LT, QUANT>;
-  const size_t smem = v_smem_bytes(kVMaxHeads);
-  const int slot = 4 + (QUANT ? 0 : (sizeof(LT) == 4 ? 1 : (std::is_same<LT, __half>::value ? 2 : 3)));
+  const size_t smem = v_smem_bytes();
+  const int slot = 12 + (QUANT ? 0 : (sizeof(LT) == 4 ? 1 : (std::is_same<LT, __half>::value ? 2 : 3)));
   int rc = ensure_smem(kern, smem, slot);
   if (rc) return rc;
   dim3 grid(nsplit, vp.lay.num_v_blocks, vp.lay.batch);
@@ -270,6 +284,7 @@ int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp
   kp.G = g.G;
   kp.rmax = g.rmax;
   kp.bsum = g.bsum;
+  kp.pitch16max = g.pitch16max;
   kp.inv_freq = a->inv_freq;
   kp.trace = g_trace;
   kp.trace_jobs = g_trace_jobs;
@@ -434,6 +449,7 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   vp.nsplit_k = ns;
   vp.tps = kp.tps;
   vp.rv_max = max_v_rank(*lay);
+  vp.err = kp.err;
   rc = dispatch_v(vp, ns, st);
   if (rc) return rc;
   if (ev) cudaEventRecord(ev[2], st);

@@ -3,12 +3,13 @@
 // LlamaLoRaAttention_headwise.py:126-133 / model.py:482-487; bx_quant._bx_fwd,
 // bx_quant.py:38-114), then the V up-projection once per head.
 //
-// int4 V with per-token groups of 32 (scale s, zero z): for a head with weights p_l,
-//   sum_l p_l x_hat[l, c] = sum_l (p_l s_lg) q_lc + sum_l p_l z_lg      (g = c / 32)
-// so each token costs one multiply per (head, group) plus one FMA per (head, channel),
-// and the zero point is one accumulator per (head, group).
+// The contraction runs on the tensor cores: int4 codes are dequantised
+// (q*s + z, one fp16 rounding) straight into an MN-major fp16 A tile, the softmax
+// weights of the block's heads form the K-major B tile, and D[channel, head]
+// accumulates in TMEM over the split.
 #pragma once
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace starkv {
 
@@ -20,33 +21,67 @@ struct VParams {
   const void* v_cache;
   const __half2* v_params;
   float* partial;        // decode: (B, Hq, nsplit, rv_max); bx mode: (B, Hq, R)
+  int* err;
   int T, nsplit, nsplit_k, tps, rv_max;
 };
 
 constexpr int kVThreads = 256;
-constexpr int kVChunk = 64;
-constexpr int kVMaxHeads = 8;
+constexpr int kVTile = 64;       // tokens per MMA step (K of the MMA)
+constexpr int kVMaxHeads = 8;    // query heads of one V block (N of the MMA, padded to 16)
+constexpr int kVMaxRank = 256;   // V block rank (M of the MMA: two 128-row tiles)
+constexpr int kVHeader = 1024;
+constexpr float kVPScale = 4096.f;   // softmax weights enter the MMA as fp16(p * 2^12)
 
-__host__ __device__ inline size_t v_smem_bytes(int heads) {
-  return (size_t)kVMaxHeads * 2 * sizeof(float) + (size_t)heads * kVChunk * sizeof(float) +
-         (size_t)kVThreads * heads * 8 * sizeof(float);
+// A tile (one buffer): 2 M-tiles x [16 channel blocks of 8][8 token blocks of 8] fp16 core
+// matrices (MN-major, no swizzle): element (c, l) of M-tile mt at
+//   mt*16384 + (c%128/8)*1024 + (l/8)*128 + (l%8)*16 + (c%8)*2.
+// B tile: [2 head blocks of 8][8 token blocks] (K-major): (g, l) at (g/8)*1024 + (l/8)*128 + (g%8)*16 + (l%8)*2.
+constexpr int kVABytes = 2 * 16384;
+constexpr int kVBBytes = 2048;
+
+__host__ __device__ inline size_t v_smem_bytes() { return (size_t)kVHeader + 2 * (kVABytes + kVBBytes); }
+
+// Instruction descriptor, kind::f16: A MN-major, B K-major, D f32, M=128, N=16.
+__host__ __device__ constexpr uint32_t idesc_v() {
+  return (1u << 4) | (1u << 15) | ((uint32_t)(16 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-// 8 consecutive V latents of one token row as floats.
-template <typename LT>
-__device__ __forceinline__ void load8(const LT* src, float* x) {
-  if constexpr (sizeof(LT) == 4) {
-    const float4 a = reinterpret_cast<const float4*>(src)[0], c = reinterpret_cast<const float4*>(src)[1];
-    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w; x[4] = c.x; x[5] = c.y; x[6] = c.z; x[7] = c.w;
-  } else {
-    const uint4 w = *reinterpret_cast<const uint4*>(src);
-    const LT* h = reinterpret_cast<const LT*>(&w);
+// 16 bytes of packed int4 codes (32 channels) -> 4 x 8 fp16 of q*s + z.
+__device__ __forceinline__ void dequant32_i4(const uint4 w, __half2 s2, __half2 z2, uint4* out) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  const __half2 k1024 = __half2half2(__ushort_as_half((unsigned short)0x6400));
 #pragma unroll
-    for (int k = 0; k < 8; ++k) x[k] = to_f32(h[k]);
+  for (int u = 0; u < 4; ++u) {
+    const uint32_t x = ws[u] & 0x0F0F0F0Fu, y = (ws[u] >> 4) & 0x0F0F0F0Fu;
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      // bytes: [x_i, -, y_i, -] -> fp16 pair (1024 + lo, 1024 + hi)
+      uint32_t v = __byte_perm(x, y, (uint32_t)(i | ((4 + i) << 8)));
+      v = (v & 0x000F000Fu) | 0x64006400u;
+      __half2 h = __hsub2(*reinterpret_cast<__half2*>(&v), k1024);   // exact codes
+      h = __hfma2(h, s2, z2);                                       // q*s + z, one rounding
+      o[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    out[u] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// 32 unquantised latents -> 4 x 8 fp16.
+template <typename LT>
+__device__ __forceinline__ void convert32(const LT* src, uint4* out) {
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    __align__(16) __half h[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) h[e] = __float2half_rn(to_f32(src[u * 8 + e]));
+    out[u] = *reinterpret_cast<uint4*>(h);
   }
 }
 
 // grid (nsplit, num_v_blocks, B), 256 threads.  LT = latent type (unquantised) or uint8_t (int4 codes).
+// D[c, g] = sum_l x_hat[l, c] * p[l, g] accumulates in TMEM (M = channels, N = heads) on the
+// tensor cores over the split's tokens, 64 tokens per step, double-buffered.
 template <typename LT, bool QUANT>
 __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_constant__ VParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -58,105 +93,195 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
   const int Gv = lay.v_num_kv[blk] * qpk;
   const int r = lay.v_rank[blk], vcol = lay.v_col[blk];
   const int R = lay.v_rank_total;
-  const int CG = r >> 3;                 // 8-channel column groups
-  const int NS = kVThreads / CG;         // token slots
-  const int cg = tid % CG, ts = tid / CG;
+  const int NQ = r >> 5;                 // 32-channel groups
+  const int MT = (r + 127) >> 7;         // 128-channel M-tiles
   const int t_begin = split * p.tps, t_end = min(p.T, t_begin + p.tps);
+  const int ntiles = t_end > t_begin ? (t_end - t_begin + kVTile - 1) / kVTile : 0;
 
-  float* s_mx = reinterpret_cast<float*>(smem);           // [8]
-  float* s_il = s_mx + kVMaxHeads;                         // [8]
-  float* s_p = s_il + kVMaxHeads;                          // [Gv][64]
-  float* s_red = s_p + Gv * kVChunk;                       // [NS * CG][Gv][8]
+  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(smem);         // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 64);
+  volatile int* s_fail = reinterpret_cast<volatile int*>(smem + 68);
+  float* s_mx = reinterpret_cast<float*>(smem + 128);             // [8]
+  float* s_il = reinterpret_cast<float*>(smem + 160);             // [8]
+  uint8_t* Abuf = smem + kVHeader;                                 // [2][kVABytes]
+  uint8_t* Bbuf = Abuf + 2 * kVABytes;                             // [2][kVBBytes]
 
-  if (!p.probs) {
-    if (warp < Gv) {
-      const int qh = qh0 + warp;
-      float m = kNegBig, l = 0.f;
-      for (int s = lane; s < p.nsplit_k; s += 32) {
-        const float2 st = p.stats[((int64_t)b * Hq + qh) * p.nsplit_k + s];
-        softmax_merge(m, l, st.x, st.y);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
-        softmax_merge(m, l, m2, l2);
-      }
-      if (lane == 0) { s_mx[warp] = m; s_il[warp] = l > 0.f ? 1.f / l : 0.f; }
-    }
+  // zero both A/B buffers once: padding channels / heads stay zero
+  for (int e = tid; e < (2 * (kVABytes + kVBBytes)) / 16; e += kVThreads)
+    reinterpret_cast<uint4*>(Abuf)[e] = make_uint4(0u, 0u, 0u, 0u);
+  if (tid == 0) {
+    mbar_init(mma_bar + 0, 1);
+    mbar_init(mma_bar + 1, 1);
+    *s_fail = 0;
+    fence_mbar_init();
   }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 32);
+    tmem_relinquish();
+  }
+  if (!p.probs && warp < Gv) {
+    const int qh = qh0 + warp;
+    float m = kNegBig, l = 0.f;
+    for (int s = lane; s < p.nsplit_k; s += 32) {
+      const float2 st = p.stats[((int64_t)b * Hq + qh) * p.nsplit_k + s];
+      softmax_merge(m, l, st.x, st.y);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
+      softmax_merge(m, l, m2, l2);
+    }
+    if (lane == 0) { s_mx[warp] = m; s_il[warp] = l > 0.f ? kVPScale / l : 0.f; }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
 
-  float acc[kVMaxHeads][8];
-  float zacc[kVMaxHeads];
-#pragma unroll
-  for (int g = 0; g < kVMaxHeads; ++g) {
-    zacc[g] = 0.f;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc[g][k] = 0.f;
-  }
+  // ---- per-thread work items of one 64-token tile
+  // codes: item i -> token lo = i%8 + 8*(i/(8*NQ)), group q = (i/8)%NQ   (NQ*64 items)
+  // weights: item i < 8*Gv -> head g = i/8, tokens 8*(i%8) .. +7
+  const int n_items = NQ * kVTile;
+  constexpr int kMaxItems = (kVMaxRank / 32) * kVTile / kVThreads;   // 2
+  constexpr int CB = QUANT ? 16 : 32 * (int)sizeof(LT);              // bytes of 32 channels
+  constexpr int CW = CB / 16;                                         // uint4 per item
+  uint4 cw[kMaxItems][CW];
+  __half2 sz[kMaxItems];
+  float lg[8];
 
-  for (int c0 = t_begin; c0 < t_end; c0 += kVChunk) {
-    for (int e = tid; e < Gv * kVChunk; e += kVThreads) {
-      const int t = e % kVChunk, g = e / kVChunk, l = c0 + t;
-      float pv = 0.f;
-      if (l < t_end) {
-        const int64_t idx = ((int64_t)b * Hq + qh0 + g) * p.T + l;
-        pv = p.probs ? p.probs[idx] : exp2f(p.logits[idx] - s_mx[g]) * s_il[g];
-      }
-      s_p[g * kVChunk + t] = pv;
-    }
-    __syncthreads();
-    if (ts < NS) {
-      const int nt = min(kVChunk, t_end - c0);
-      for (int t = ts; t < nt; t += NS) {
-        const int64_t row = (int64_t)b * lay.capacity + c0 + t;
-        float x[8];
-        float s = 1.f, z = 0.f;
-        if constexpr (QUANT) {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint8_t*>(p.v_cache) +
-                                                                row * (R / 2) + vcol / 2 + cg * 4);
+  auto load_tile = [&](int t) {
+    const int t0 = t_begin + t * kVTile;
 #pragma unroll
-          for (int k = 0; k < 8; ++k) x[k] = (float)((w >> (4 * k)) & 15u);
-          const float2 sz = __half22float2(p.v_params[row * (R / 32) + vcol / 32 + cg / 4]);
-          s = sz.x;
-          z = sz.y;
-        } else {
-          load8<LT>(reinterpret_cast<const LT*>(p.v_cache) + row * R + vcol + cg * 8, x);
-        }
+    for (int it = 0; it < kMaxItems; ++it) {
+      const int i = tid + it * kVThreads;
+      if (i < n_items) {
+        const int lo = (i & 7) + 8 * (i / (8 * NQ)), q = (i >> 3) % NQ;
+        const int l = t0 + lo;
+        if (l < t_end) {
+          const int64_t row = (int64_t)b * lay.capacity + l;
+          if constexpr (QUANT) {
+            cw[it][0] = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.v_cache) + row * (R / 2) +
+                                                        vcol / 2 + q * 16);
+            sz[it] = p.v_params[row * (R / 32) + vcol / 32 + q];
+          } else {
+            const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const LT*>(p.v_cache) + row * R + vcol + q * 32);
 #pragma unroll
-        for (int g = 0; g < kVMaxHeads; ++g) {
-          if (g < Gv) {
-            const float pv = s_p[g * kVChunk + t];
-            const float ps = QUANT ? pv * s : pv;
-            if (QUANT) zacc[g] = fmaf(pv, z, zacc[g]);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) acc[g][k] = fmaf(ps, x[k], acc[g][k]);
+            for (int u = 0; u < CW; ++u) cw[it][u] = src[u];
           }
+        } else {
+#pragma unroll
+          for (int u = 0; u < CW; ++u) cw[it][u] = make_uint4(0u, 0u, 0u, 0u);
+          sz[it] = __floats2half2_rn(0.f, 0.f);
         }
       }
     }
-    __syncthreads();
-  }
+    if (tid < 8 * Gv) {
+      const int g = tid >> 3, l0 = t0 + 8 * (tid & 7);
+      const int64_t base = ((int64_t)b * Hq + qh0 + g) * p.T;
+      const float* src = p.probs ? p.probs : p.logits;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) lg[e] = (l0 + e < t_end) ? src[base + l0 + e] : 0.f;
+    }
+  };
 
-  // reduce over token slots
-  if (ts < NS) {
+  auto store_tile = [&](int t, int buf) {
+    uint8_t* A = Abuf + buf * kVABytes;
+    uint8_t* Bm = Bbuf + buf * kVBBytes;
 #pragma unroll
-    for (int g = 0; g < kVMaxHeads; ++g)
-      if (g < Gv)
+    for (int it = 0; it < kMaxItems; ++it) {
+      const int i = tid + it * kVThreads;
+      if (i < n_items) {
+        const int lo = (i & 7) + 8 * (i / (8 * NQ)), q = (i >> 3) % NQ;
+        uint4 o[4];
+        if constexpr (QUANT) {
+          dequant32_i4(cw[it][0], __half2half2(__low2half(sz[it])), __half2half2(__high2half(sz[it])), o);
+        } else {
+          convert32<LT>(reinterpret_cast<const LT*>(&cw[it][0]), o);
+        }
 #pragma unroll
-        for (int k = 0; k < 8; ++k) s_red[((size_t)tid * Gv + g) * 8 + k] = acc[g][k] + zacc[g];
+        for (int u = 0; u < 4; ++u) {
+          const int c = q * 32 + u * 8;
+          *reinterpret_cast<uint4*>(A + (c >> 7) * 16384 + ((c & 127) >> 3) * 1024 + (lo >> 3) * 128 + (lo & 7) * 16) = o[u];
+        }
+      }
+    }
+    if (tid < 8 * Gv) {
+      const int g = tid >> 3, kb = tid & 7;
+      const int l0 = t_begin + t * kVTile + 8 * kb;
+      __align__(16) __half h[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float pv = 0.f;
+        if (l0 + e < t_end) pv = p.probs ? lg[e] * kVPScale : exp2f(lg[e] - s_mx[g]) * s_il[g];
+        h[e] = __float2half_rn(pv);
+      }
+      *reinterpret_cast<uint4*>(Bm + (g >> 3) * 1024 + kb * 128 + (g & 7) * 16) = *reinterpret_cast<uint4*>(h);
+    }
+  };
+
+  constexpr uint32_t IDESC = idesc_v();
+  if (ntiles > 0) load_tile(0);
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    if (t >= 2) {
+      // the MMAs of tile t-2 read this buffer
+      int fail = !mbar_wait(mma_bar + buf, (uint32_t)(((t - 2) >> 1) & 1));
+      if (fail) { record_error(p.err, kDevWaitMma); *s_fail = 1; }
+    }
+    if (__syncthreads_or(*s_fail)) break;
+    store_tile(t, buf);
+    if (t + 1 < ntiles) load_tile(t + 1);
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(Abuf + buf * kVABytes), b0 = smem_u32(Bbuf + buf * kVBBytes);
+      for (int mt = 0; mt < MT; ++mt)
+        for (int ks = 0; ks < kVTile / 16; ++ks)
+          mma_f16_ss(tmem + mt * 16, smem_desc(a0 + mt * 16384 + ks * 256, 128, 1024),
+                     smem_desc(b0 + ks * 256, 128, 1024), IDESC, (t > 0 || ks > 0) ? 1u : 0u);
+      mma_commit(mma_bar + buf);
+    }
+  }
+  // ---- wait for the last MMAs, read D[c, g] and write the partials
+  if (tid == 0 && ntiles > 0 && !*s_fail) {
+    const int t = ntiles - 1;
+    if (!mbar_wait(mma_bar + (t & 1), (uint32_t)((t >> 1) & 1))) { record_error(p.err, kDevWaitMma); *s_fail = 1; }
   }
   __syncthreads();
-  for (int e = tid; e < Gv * r; e += kVThreads) {
-    const int g = e / r, c = e % r;
-    const int ccg = c >> 3, k = c & 7;
-    float sum = 0.f;
-    for (int s = 0; s < NS; ++s) sum += s_red[((size_t)(s * CG + ccg) * Gv + g) * 8 + k];
-    const int qh = qh0 + g;
-    if (p.probs)
-      p.partial[((int64_t)b * Hq + qh) * R + vcol + c] = sum;
-    else
-      p.partial[(((int64_t)b * Hq + qh) * p.nsplit + split) * p.rv_max + c] = sum;
+  tc_fence_after();
+  if (warp < 4 * MT && !*s_fail) {
+    const int mt = warp >> 2, cq = warp & 3;
+    const int c = mt * 128 + cq * 32 + lane;
+    float d[16];
+    if (ntiles > 0) {
+      float dd[16];
+      tmem_ld16x2(tmem + ((uint32_t)(cq * 32) << 16) + mt * 16, tmem + ((uint32_t)(cq * 32) << 16) + mt * 16, d, dd);
+    } else {
+#pragma unroll
+      for (int g = 0; g < 16; ++g) d[g] = 0.f;
+    }
+    if (c < r) {
+#pragma unroll
+      for (int g = 0; g < kVMaxHeads; ++g) {
+        if (g < Gv) {
+          const int qh = qh0 + g;
+          const float v = d[g] * (1.f / kVPScale);
+          if (p.probs)
+            p.partial[((int64_t)b * Hq + qh) * R + vcol + c] = v;
+          else
+            p.partial[(((int64_t)b * Hq + qh) * p.nsplit + split) * p.rv_max + c] = v;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
   }
 }
 
