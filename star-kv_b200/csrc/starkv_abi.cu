@@ -184,10 +184,10 @@ int validate(const starkv_layout* lp) {
   int vcol = 0, kv = 0;
   for (int j = 0; j < l.num_v_blocks; ++j) {
     const int r = l.v_rank[j];
-    if (r <= 0 || r % 32 || r > 256) return set_error(STARKV_ERR_UNSUPPORTED, "V rank must be a multiple of 32 in [32, 256]");
+    if (r <= 0 || r % 32 || r > kVMaxRank) return set_error(STARKV_ERR_UNSUPPORTED, "V rank must be a multiple of 32 in [32, 1024]");
     if (l.v_col[j] != vcol) return set_error(STARKV_ERR_INVALID, "v_col is not the prefix sum of v_rank");
     if (l.v_first_kv[j] != kv || l.v_num_kv[j] <= 0) return set_error(STARKV_ERR_INVALID, "V blocks must tile the KV heads in order");
-    if (l.v_num_kv[j] * qpk > kVMaxHeads) return set_error(STARKV_ERR_UNSUPPORTED, "more than 8 query heads in a V block");
+    if (l.v_num_kv[j] * qpk > kVMaxHeads) return set_error(STARKV_ERR_UNSUPPORTED, "more than 32 query heads in a V block");
     vcol += r;
     kv += l.v_num_kv[j];
   }
@@ -247,8 +247,10 @@ int launch_v(const VParams& vp, int nsplit, cudaStream_t st) {
   const int slot = 12 + (QUANT ? 0 : (sizeof(LT) == 4 ? 1 : (std::is_same<LT, __half>::value ? 2 : 3)));
   int rc = ensure_smem(kern, smem, slot);
   if (rc) return rc;
-  dim3 grid(nsplit, vp.lay.num_v_blocks, vp.lay.batch);
-  kern<<<grid, kVThreads, smem, st>>>(vp);
+  VParams v2 = vp;
+  v2.ctiles = (max_v_rank(vp.lay) + kVCtaRank - 1) / kVCtaRank;
+  dim3 grid(nsplit, vp.lay.num_v_blocks * v2.ctiles, vp.lay.batch);
+  kern<<<grid, kVThreads, smem, st>>>(v2);
   return fail_launch();
 }
 

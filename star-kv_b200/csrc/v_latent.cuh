@@ -23,27 +23,29 @@ struct VParams {
   float* partial;        // decode: (B, Hq, nsplit, rv_max); bx mode: (B, Hq, R)
   int* err;
   int T, nsplit, nsplit_k, tps, rv_max;
+  int ctiles;            // channel tiles of kVCtaRank per V block (grid.y = blocks * ctiles)
 };
 
 constexpr int kVThreads = 256;
 constexpr int kVTile = 64;       // tokens per MMA step (K of the MMA)
-constexpr int kVMaxHeads = 8;    // query heads of one V block (N of the MMA, padded to 16)
-constexpr int kVMaxRank = 256;   // V block rank (M of the MMA: two 128-row tiles)
+constexpr int kVMaxHeads = 32;   // query heads of one V block (N of the MMA, padded to 32)
+constexpr int kVCtaRank = 256;   // channels of a V block one CTA covers (two 128-row M tiles)
+constexpr int kVMaxRank = 1024;  // V block rank (the reference's global V is one block)
 constexpr int kVHeader = 1024;
 constexpr float kVPScale = 4096.f;   // softmax weights enter the MMA as fp16(p * 2^12)
 
 // A tile (one buffer): 2 M-tiles x [16 channel blocks of 8][8 token blocks of 8] fp16 core
 // matrices (MN-major, no swizzle): element (c, l) of M-tile mt at
 //   mt*16384 + (c%128/8)*1024 + (l/8)*128 + (l%8)*16 + (c%8)*2.
-// B tile: [2 head blocks of 8][8 token blocks] (K-major): (g, l) at (g/8)*1024 + (l/8)*128 + (g%8)*16 + (l%8)*2.
+// B tile: [4 head blocks of 8][8 token blocks] (K-major): (g, l) at (g/8)*1024 + (l/8)*128 + (g%8)*16 + (l%8)*2.
 constexpr int kVABytes = 2 * 16384;
-constexpr int kVBBytes = 2048;
+constexpr int kVBBytes = 4096;
 
 __host__ __device__ inline size_t v_smem_bytes() { return (size_t)kVHeader + 2 * (kVABytes + kVBBytes); }
 
-// Instruction descriptor, kind::f16: A MN-major, B K-major, D f32, M=128, N=16.
+// Instruction descriptor, kind::f16: A MN-major, B K-major, D f32, M=128, N=32.
 __host__ __device__ constexpr uint32_t idesc_v() {
-  return (1u << 4) | (1u << 15) | ((uint32_t)(16 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+  return (1u << 4) | (1u << 15) | ((uint32_t)(32 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
 // 16 bytes of packed int4 codes (32 channels) -> 4 x 8 fp16 of q*s + z.
@@ -79,19 +81,23 @@ __device__ __forceinline__ void convert32(const LT* src, uint4* out) {
   }
 }
 
-// grid (nsplit, num_v_blocks, B), 256 threads.  LT = latent type (unquantised) or uint8_t (int4 codes).
+// grid (nsplit, num_v_blocks * channel tiles of 256, B), 256 threads.  LT = latent type (unquantised) or uint8_t (int4 codes).
 // D[c, g] = sum_l x_hat[l, c] * p[l, g] accumulates in TMEM (M = channels, N = heads) on the
 // tensor cores over the split's tokens, 64 tokens per step, double-buffered.
 template <typename LT, bool QUANT>
 __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_constant__ VParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const starkv_layout& lay = p.lay;
-  const int split = blockIdx.x, blk = blockIdx.y, b = blockIdx.z;
+  const int split = blockIdx.x, b = blockIdx.z;
+  const int blk = blockIdx.y / p.ctiles, ct = blockIdx.y % p.ctiles;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int Hq = lay.num_q_heads, qpk = Hq / lay.num_kv_heads;
   const int qh0 = lay.v_first_kv[blk] * qpk;
   const int Gv = lay.v_num_kv[blk] * qpk;
-  const int r = lay.v_rank[blk], vcol = lay.v_col[blk];
+  const int c_lo = ct * kVCtaRank;                                  // first channel of this CTA
+  if (c_lo >= lay.v_rank[blk]) return;
+  const int r = min(kVCtaRank, lay.v_rank[blk] - c_lo);            // channels of this CTA
+  const int vcol = lay.v_col[blk] + c_lo;                           // global column of channel 0
   const int R = lay.v_rank_total;
   const int NQ = r >> 5;                 // 32-channel groups
   const int MT = (r + 127) >> 7;         // 128-channel M-tiles
@@ -101,8 +107,8 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
   uint64_t* mma_bar = reinterpret_cast<uint64_t*>(smem);         // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 64);
   volatile int* s_fail = reinterpret_cast<volatile int*>(smem + 68);
-  float* s_mx = reinterpret_cast<float*>(smem + 128);             // [8]
-  float* s_il = reinterpret_cast<float*>(smem + 160);             // [8]
+  float* s_mx = reinterpret_cast<float*>(smem + 256);             // [32]
+  float* s_il = reinterpret_cast<float*>(smem + 384);             // [32]
   uint8_t* Abuf = smem + kVHeader;                                 // [2][kVABytes]
   uint8_t* Bbuf = Abuf + 2 * kVABytes;                             // [2][kVBBytes]
 
@@ -116,11 +122,11 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(tmem_slot, 32);
+    tmem_alloc(tmem_slot, 64);
     tmem_relinquish();
   }
-  if (!p.probs && warp < Gv) {
-    const int qh = qh0 + warp;
+  for (int gw = warp; !p.probs && gw < Gv; gw += kVThreads / 32) {
+    const int qh = qh0 + gw;
     float m = kNegBig, l = 0.f;
     for (int s = lane; s < p.nsplit_k; s += 32) {
       const float2 st = p.stats[((int64_t)b * Hq + qh) * p.nsplit_k + s];
@@ -131,7 +137,7 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
       const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
       softmax_merge(m, l, m2, l2);
     }
-    if (lane == 0) { s_mx[warp] = m; s_il[warp] = l > 0.f ? kVPScale / l : 0.f; }
+    if (lane == 0) { s_mx[gw] = m; s_il[gw] = l > 0.f ? kVPScale / l : 0.f; }
   }
   fence_proxy_async_smem();
   tc_fence_before();
@@ -143,7 +149,7 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
   // codes: item i -> token lo = i%8 + 8*(i/(8*NQ)), group q = (i/8)%NQ   (NQ*64 items)
   // weights: item i < 8*Gv -> head g = i/8, tokens 8*(i%8) .. +7
   const int n_items = NQ * kVTile;
-  constexpr int kMaxItems = (kVMaxRank / 32) * kVTile / kVThreads;   // 2
+  constexpr int kMaxItems = (kVCtaRank / 32) * kVTile / kVThreads;   // 2
   constexpr int CB = QUANT ? 16 : 32 * (int)sizeof(LT);              // bytes of 32 channels
   constexpr int CW = CB / 16;                                         // uint4 per item
   uint4 cw[kMaxItems][CW];
@@ -240,7 +246,7 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
       const uint32_t a0 = smem_u32(Abuf + buf * kVABytes), b0 = smem_u32(Bbuf + buf * kVBBytes);
       for (int mt = 0; mt < MT; ++mt)
         for (int ks = 0; ks < kVTile / 16; ++ks)
-          mma_f16_ss(tmem + mt * 16, smem_desc(a0 + mt * 16384 + ks * 256, 128, 1024),
+          mma_f16_ss(tmem + mt * 32, smem_desc(a0 + mt * 16384 + ks * 256, 128, 1024),
                      smem_desc(b0 + ks * 256, 128, 1024), IDESC, (t > 0 || ks > 0) ? 1u : 0u);
       mma_commit(mma_bar + buf);
     }
@@ -255,13 +261,13 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
   if (warp < 4 * MT && !*s_fail) {
     const int mt = warp >> 2, cq = warp & 3;
     const int c = mt * 128 + cq * 32 + lane;
-    float d[16];
+    float d[32];
     if (ntiles > 0) {
-      float dd[16];
-      tmem_ld16x2(tmem + ((uint32_t)(cq * 32) << 16) + mt * 16, tmem + ((uint32_t)(cq * 32) << 16) + mt * 16, d, dd);
+      tmem_ld16x2(tmem + ((uint32_t)(cq * 32) << 16) + mt * 32, tmem + ((uint32_t)(cq * 32) << 16) + mt * 32 + 16, d,
+                  d + 16);
     } else {
 #pragma unroll
-      for (int g = 0; g < 16; ++g) d[g] = 0.f;
+      for (int g = 0; g < 32; ++g) d[g] = 0.f;
     }
     if (c < r) {
 #pragma unroll
@@ -272,7 +278,7 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
           if (p.probs)
             p.partial[((int64_t)b * Hq + qh) * R + vcol + c] = v;
           else
-            p.partial[(((int64_t)b * Hq + qh) * p.nsplit + split) * p.rv_max + c] = v;
+            p.partial[(((int64_t)b * Hq + qh) * p.nsplit + split) * p.rv_max + c_lo + c] = v;
         }
       }
     }
@@ -281,7 +287,7 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, 32);
+    tmem_dealloc(tmem, 64);
   }
 }
 
@@ -297,7 +303,7 @@ struct CombineParams {
 };
 
 __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ CombineParams p) {
-  __shared__ float o_lat[256];
+  __shared__ float o_lat[kVMaxRank];
   const starkv_layout& lay = p.lay;
   const int qh = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
   const int Hq = lay.num_q_heads, qpk = Hq / lay.num_kv_heads, kv = qh / qpk;

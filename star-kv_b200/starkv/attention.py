@@ -1,0 +1,234 @@
+"""Drop-in ``LlamaCustomAttention`` modules backed by libstarkv.
+
+Same constructor, attributes and forward signatures as the reference's
+``LlamaLoRaAttention_headwise.LlamaCustomAttention`` (headwise.py:32-148) and
+``LlamaLoRaAttention_headwise_quant.LlamaCustomAttention`` (quant.py:38-202):
+``q_proj``/``o_proj`` linears, ``k_proj.VS`` / ``k_proj.U`` (``[Hkv, 128, r]``) and
+``v_proj.VS`` / ``v_proj.U`` (``Linear[Hkv*128, rv]``) as produced by the reference's
+export (model.py:286-380), ``forward(hidden_states, position_embeddings,
+attention_mask, position_ids, past_key_values, cache_position)`` returning
+``(attn_output, None)``.
+
+Decode steps (one query token) run the fused B200 path: the new token's latents
+are appended to the cache and ``starkv_decode_attention`` computes the per-head
+outputs, which go through ``o_proj``.  Two caches are accepted as
+``past_key_values``:
+
+* ``StarKVCache`` — the preallocated latent cache of this package (in-place
+  append; int8/int4 codes for the quantised module);
+* an HF ``Cache`` (e.g. ``DynamicCache``) — its ``update`` is called exactly as
+  the reference does (headwise.py:99) and the decode kernels run directly on the
+  returned ``(B, Hkv, L, r)`` / ``(B, L, rv)`` latent tensors (unquantised).
+
+Prompt steps (more than one query token) store the latents in the cache and
+compute the prompt's attention on the GPU with torch SDPA on the reconstructed
+keys/values, as the reference's own prefill branch does (model.py:429-449).
+
+RoPE: the query is rotated with the supplied ``position_embeddings`` exactly as
+``apply_rotary_pos_emb_custom`` (headwise.py:22-29); cached keys are rotated by
+their slot positions inside the kernel, with ``inv_freq`` from the config's
+``rope_theta`` (the reference's HF default rope).
+"""
+
+from __future__ import annotations
+
+from typing import Dict, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+from .layer import DecodeLayer, rope_inv_freq
+
+
+def rotate_half(x: torch.Tensor) -> torch.Tensor:
+    h = x.shape[-1] // 2
+    return torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+
+
+def apply_rotary_pos_emb_custom(x, cos, sin, unsqueeze_dim=1):
+    """The reference's RoPE helper (headwise.py:22-29): when the tables do not
+    match the sequence length, the last table row is used."""
+    cos = cos.unsqueeze(unsqueeze_dim)
+    sin = sin.unsqueeze(unsqueeze_dim)
+    if x.shape[-2] != cos.shape[-2]:
+        cos = cos[:, :, -1, :].unsqueeze(2)
+        sin = sin[:, :, -1, :].unsqueeze(2)
+    return (x * cos) + (rotate_half(x) * sin)
+
+
+class StarKVCache:
+    """Preallocated per-layer latent caches (the static replacement of the
+    reference's ``DynamicCache`` for the drop-in modules).
+
+    capacity: token slots per sequence; quantized: int8 K / int4 V codes."""
+
+    def __init__(self, capacity: int, quantized: bool = False):
+        self.capacity = int(capacity)
+        self.quantized = bool(quantized)
+        self.layers: Dict[int, DecodeLayer] = {}
+
+    def get_seq_length(self, layer_idx: int = 0) -> int:
+        st = self.layers.get(layer_idx)
+        return 0 if st is None else st.length
+
+    def layer(self, layer_idx: int, module: "LlamaCustomAttention", batch: int, dtype: torch.dtype) -> DecodeLayer:
+        st = self.layers.get(layer_idx)
+        if st is None:
+            lay = ops.make_layout(batch, module.num_heads, module.num_key_value_heads, module.k_ranks(),
+                                  [module.v_rank()], [module.num_key_value_heads], self.capacity,
+                                  self.quantized, dtype)
+            st = DecodeLayer(lay, module.packed_k_u(dtype), module.v_proj.U.weight.to(dtype).contiguous(),
+                             module.rope_theta)
+            self.layers[layer_idx] = st
+        return st
+
+
+class LlamaCustomAttention(nn.Module):
+    """Llama attention with low-rank (SVD-factored) K/V projections whose latent
+    cache is decoded by the B200 kernels.  ``quantized`` selects the int8 K /
+    int4 V cache of the quantised module."""
+
+    quantized = False
+
+    def __init__(self, config, layer_idx: Optional[int] = None, decomp_goup_num: Optional[int] = 1):
+        super().__init__()
+        self.config = config
+        self.layer_idx = layer_idx
+        self.attention_dropout = config.attention_dropout
+        self.hidden_size = config.hidden_size
+        self.num_heads = config.num_attention_heads
+        self.head_dim = self.hidden_size // self.num_heads
+        self.num_key_value_heads = config.num_key_value_heads
+        self.num_key_value_groups = self.num_heads // self.num_key_value_heads
+        self.max_position_embeddings = config.max_position_embeddings
+        rp = getattr(config, "rope_parameters", None) or {}
+        self.rope_theta = float(getattr(config, "rope_theta", None) or rp.get("rope_theta", 10000.0))
+        self.is_causal = True
+        self.scaling = self.head_dim ** -0.5
+        bias = config.attention_bias
+        self.q_proj = nn.Linear(self.hidden_size, self.num_heads * self.head_dim, bias=bias)
+        self.k_proj = nn.Linear(self.hidden_size, self.num_key_value_heads * self.head_dim, bias=bias)
+        self.v_proj = nn.Linear(self.hidden_size, self.num_key_value_heads * self.head_dim, bias=bias)
+        self.o_proj = nn.Linear(self.num_heads * self.head_dim, self.hidden_size, bias=bias)
+        self.decomp_goup_num = decomp_goup_num
+        self.decomp_goup_num_kv = decomp_goup_num // self.num_key_value_groups
+        self._u_cache = None
+
+    # ---- weight views in the layouts the kernels consume
+    def k_ranks(self):
+        r = int(self.k_proj.U.shape[-1])
+        return [r] * self.num_key_value_heads
+
+    def v_rank(self) -> int:
+        return int(self.v_proj.U.weight.shape[1])
+
+    def packed_k_u(self, dtype) -> torch.Tensor:
+        """k_proj.U as (Hkv, 128, r) contiguous == the packed per-head layout."""
+        u = self.k_proj.U
+        key = (u.data_ptr(), dtype)
+        if self._u_cache is None or self._u_cache[0] != key:
+            self._u_cache = (key, u.to(dtype).contiguous().reshape(-1))
+        return self._u_cache[1]
+
+    # ---- forward
+    def forward(self, hidden_states, position_embeddings, attention_mask, position_ids=None, past_key_values=None,
+                cache_position=None, **kwargs):
+        B, q_len, _ = hidden_states.shape
+        dt = hidden_states.dtype
+        Hq, Hkv, D = self.num_heads, self.num_key_value_heads, self.head_dim
+        q = self.q_proj(hidden_states).view(B, q_len, Hq, D).transpose(1, 2)
+        cos, sin = position_embeddings
+        q = apply_rotary_pos_emb_custom(q, cos, sin)
+        k_lat = torch.matmul(hidden_states, self.k_proj.VS.weight.T)          # (B, q, Hkv*r)
+        v_lat = torch.matmul(hidden_states, self.v_proj.VS.weight.T)          # (B, q, rv)
+        r = self.k_ranks()[0]
+
+        if isinstance(past_key_values, StarKVCache):
+            st = past_key_values.layer(self.layer_idx, self, B, dt)
+            if q_len == 1:
+                mask = self._decode_mask(attention_mask, B, st.length + 1)
+                out = st.step(q[:, :, 0, :], k_lat.contiguous(), v_lat.contiguous(), mask=mask)
+                return self.o_proj(out.reshape(B, 1, Hq * D)), None
+            if st.length != 0:
+                raise NotImplementedError("multi-token steps after the prompt are not supported by the decode path")
+            st.prefill(k_lat.contiguous(), v_lat.contiguous())
+            keys, values = k_lat.view(B, q_len, Hkv, r).transpose(1, 2), v_lat
+        elif past_key_values is not None:
+            keys, values = past_key_values.update(k_lat.view(B, q_len, Hkv, r).transpose(1, 2), v_lat,
+                                                  self.layer_idx)
+            if q_len == 1:
+                out = self._decode_on_tensors(q[:, :, 0, :], keys, values, attention_mask)
+                return self.o_proj(out.reshape(B, 1, Hq * D)), None
+        else:
+            keys, values = k_lat.view(B, q_len, Hkv, r).transpose(1, 2), v_lat
+            if q_len == 1:
+                out = self._decode_on_tensors(q[:, :, 0, :], keys, values, attention_mask)
+                return self.o_proj(out.reshape(B, 1, Hq * D)), None
+        out = self._prompt_attention(q, keys, values, cos, sin, attention_mask)
+        return self.o_proj(out.transpose(1, 2).reshape(B, q_len, Hq * D)), None
+
+    # ---- helpers
+    @staticmethod
+    def _decode_mask(attention_mask, B, L):
+        if attention_mask is None:
+            return None
+        m = attention_mask[:, 0, -1, :L] if attention_mask.dim() == 4 else attention_mask[:, :L]
+        return m.to(torch.float32).expand(B, L).contiguous()
+
+    def _decode_on_tensors(self, q_rot, keys, values, attention_mask):
+        """Decode over an HF cache's latent tensors (B, Hkv, L, r) / (B, L, rv) in place."""
+        B, Hkv, L, r = keys.shape
+        keys = keys.contiguous()
+        values = values.contiguous()
+        dt = keys.dtype
+        lay = ops.make_layout(B, self.num_heads, Hkv, [r] * Hkv, [values.shape[-1]], [Hkv], L, False, dt,
+                              k_offsets=[h * L * r for h in range(Hkv)], k_batch_strides=[Hkv * L * r] * Hkv)
+        cache = ops.LatentCache.__new__(ops.LatentCache)
+        cache.layout, cache.k_cache, cache.k_scales = lay, keys.reshape(-1), None
+        cache.v_cache, cache.v_params, cache.length = values, None, L
+        inv = getattr(self, "_inv_freq", None)
+        if inv is None or inv.device != keys.device:
+            inv = self._inv_freq = rope_inv_freq(self.rope_theta, 128, keys.device)
+        return ops.decode_attention(lay, cache, q_rot.contiguous(), self.packed_k_u(dt),
+                                    self.v_proj.U.weight.to(dt).contiguous(), inv, self.scaling, L,
+                                    mask=self._decode_mask(attention_mask, B, L))
+
+    def _prompt_attention(self, q, keys, values, cos, sin, attention_mask):
+        """Prompt (q_len > 1) attention with torch SDPA on reconstructed K/V
+        (model.py:429-449)."""
+        B, Hq, Lq, D = q.shape
+        Hkv = self.num_key_value_heads
+        u = self.k_proj.U.to(keys.dtype)                                       # (Hkv, D, r)
+        k_full = torch.matmul(keys, u.transpose(-2, -1))                       # (B, Hkv, L, D)
+        k_full = apply_rotary_pos_emb_custom(k_full, cos, sin)
+        v_full = torch.matmul(values, self.v_proj.U.weight.T.to(values.dtype))
+        v_full = v_full.view(B, -1, Hkv, D).transpose(1, 2)
+        grp = self.num_key_value_groups
+        k_full = k_full.repeat_interleave(grp, dim=1)
+        v_full = v_full.repeat_interleave(grp, dim=1)
+        mask = None if attention_mask is None else attention_mask[:, :, :, :k_full.shape[-2]]
+        return F.scaled_dot_product_attention(q, k_full, v_full, attn_mask=mask, scale=self.scaling,
+                                              is_causal=mask is None and Lq > 1)
+
+
+class LlamaCustomAttentionQuant(LlamaCustomAttention):
+    """The quantised module (quant.py:38-202): int8 per-channel K codes and int4
+    per-token-group V codes in a ``StarKVCache(quantized=True)``.  The four cache
+    arguments of the reference forward are accepted; ``past_key_values_upper``
+    carries the ``StarKVCache`` (the others are unused: codes and scales live in
+    the one cache object)."""
+
+    quantized = True
+
+    def forward(self, hidden_states, position_embeddings, attention_mask, position_ids=None,
+                past_key_values_upper=None, past_key_values_lower=None, scales_upper=None, scales_lower=None,
+                cache_position=None, **kwargs):
+        cache = past_key_values_upper
+        if cache is not None and not isinstance(cache, StarKVCache):
+            raise TypeError("the quantised module takes a StarKVCache(quantized=True) as past_key_values_upper")
+        if cache is not None and not cache.quantized:
+            raise ValueError("StarKVCache must be created with quantized=True for the quantised module")
+        return super().forward(hidden_states, position_embeddings, attention_mask, position_ids,
+                               past_key_values=cache, cache_position=cache_position)

@@ -45,8 +45,10 @@ def test_layout_validation_host_only():
     assert lib.starkv_validate_layout(C.byref(bad)) == 1
     with pytest.raises(_lib.StarKVError):
         ops.make_layout(2, 8, 8, [256] * 8, [64, 64], [4, 4], 10, True, torch.float16)
-    with pytest.raises(_lib.StarKVError):                            # 16 q heads in one V block
-        ops.make_layout(1, 32, 8, [32] * 8, [64] * 2, [4, 4], 10, True, torch.float16)
+    with pytest.raises(_lib.StarKVError):                            # 64 q heads in one V block
+        ops.make_layout(1, 64, 8, [32] * 8, [64], [8], 10, True, torch.float16)
+    with pytest.raises(_lib.StarKVError):                            # V block rank above 1024
+        ops.make_layout(1, 8, 8, [32] * 8, [1056], [8], 10, True, torch.float16)
 
 
 def test_no_cpu_path():

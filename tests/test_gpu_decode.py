@@ -71,6 +71,9 @@ def test_decode_matches_reference_golden(cuda, name):
     ("c2", dict(num_q_heads=32, num_kv_heads=8, batch=2, context=2000), False),
     ("c0", dict(num_q_heads=8, batch=2, context=700, dtype="float16"), False),
     ("c0", dict(num_q_heads=8, batch=2, context=700, dtype="bfloat16"), True),
+    # V blocks with more than 8 query heads and ranks above one 256-channel CTA tile
+    ("c0", dict(num_q_heads=32, batch=1, context=300, v_block_kv=[16, 16], v_ranks=[512, 320]), False),
+    ("c1", dict(num_q_heads=32, batch=2, context=600, v_block_kv=[32], v_ranks=[1024]), False),
 ])
 def test_decode_matches_oracle(cuda, cfg, over, mask):
     spec = make_spec(cfg, seed=11, **over)
