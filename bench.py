@@ -105,27 +105,6 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-# ---------------------------------------------------------------- sharding
-def shard_spec(spec, rank: int, world: int):
-    """Heads of rank `rank`: a contiguous range of whole V blocks."""
-    import copy
-    nb = spec.num_v_blocks
-    if nb % world:
-        raise SystemExit(f"{nb} V blocks do not split over {world} GPUs")
-    per = nb // world
-    b0, b1 = rank * per, (rank + 1) * per
-    kv0 = sum(spec.v_block_kv[:b0])
-    kv1 = sum(spec.v_block_kv[:b1])
-    qpk = spec.num_q_heads // spec.num_kv_heads
-    sub = copy.deepcopy(spec)
-    sub.k_ranks = spec.k_ranks[kv0:kv1]
-    sub.v_ranks = spec.v_ranks[b0:b1]
-    sub.v_block_kv = spec.v_block_kv[b0:b1]
-    sub.num_kv_heads = kv1 - kv0
-    sub.num_q_heads = (kv1 - kv0) * qpk
-    return sub
-
-
 # ---------------------------------------------------------------- CPU arm
 def cpu_sample(spec, seed: int = 0):
     """Time the oracle port (numpy, fp32) on one sequence of the workload."""
@@ -222,26 +201,27 @@ def main():
         args.gpus = world
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
-
+    from starkv import dist as sd
     from starkv import ops
     from starkv.harness import device_layer
 
-    sub = shard_spec(spec, rank, world) if world > 1 else spec
+    if world > 1:
+        sd.init("nccl", timeout_s=300, device_id=dev)
+        sd.check_partition(spec, device=dev)
+    sub = sd.shard_spec(spec, rank, world) if world > 1 else spec
     st, _, _ = device_layer(sub, dev, seed=1 + rank)
     layer = st.layer
     layer.num_splits = args.splits
     L = sub.context
     B, hq = sub.batch, sub.num_q_heads
     out = torch.empty(B, hq, 128, dtype=st.q.dtype, device=dev)
-    gathered = torch.empty(world, B, hq, 128, dtype=st.q.dtype, device=dev) if world > 1 else None
+    gathered = torch.empty(world * B, hq, 128, dtype=st.q.dtype, device=dev) if world > 1 else None
 
     def step(events=None):
         layer.cache.length = L                      # the step rewrites slot L and attends 0..L
         layer.step(st.q, st.k_new, st.v_new, out=out, events=events)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
+            sd.gather_heads(out, buffer=gathered)
 
     for _ in range(args.warmup):
         step()
@@ -289,8 +269,8 @@ def main():
             layer.cache.length = L
             layer.step(dq, dk, dv, out=out)
             if world > 1:
-                dist.all_gather_into_tensor(gathered, out)
-                hout.copy_(gathered.view(-1), non_blocking=True)
+                full = sd.gather_heads(out, buffer=gathered)
+                hout.copy_(full.reshape(-1), non_blocking=True)
             else:
                 hout.copy_(out.view(-1), non_blocking=True)
 
