@@ -81,7 +81,7 @@ int k_elem_bytes(const starkv_layout& l) { return l.quantized ? 1 : dtype_bytes(
 // K-path geometry: heads per CTA (G) and the shared memory that fits (one CTA
 // per SM: it owns all 512 TMEM columns).
 struct KGeom {
-  int G, rmax, bsum, pitch16max;
+  int G, rmax, bsum, pitch16max, nstages;
   size_t smem;
 };
 
@@ -95,6 +95,7 @@ KGeom k_geometry(const starkv_layout& l) {
     const int pt = k_pitch16(l.k_rank[h], xb);
     g.pitch16max = pt > g.pitch16max ? pt : g.pitch16max;
   }
+  // Largest G whose W matrices leave room for a staging ring of >= 3 stages (2 at G = 1).
   for (int G = 4; G >= 1; G >>= 1) {
     if (Hq % G) continue;
     int bsum = 0;
@@ -103,10 +104,12 @@ KGeom k_geometry(const starkv_layout& l) {
       for (int k = 0; k < G; ++k) s += l.k_rank[(grp * G + k) / qpk];
       bsum = s > bsum ? s : bsum;
     }
-    const size_t bytes = k_smem_bytes(bsum, g.rmax, g.pitch16max, xb);
-    if (bytes <= 227 * 1024) {
+    const int ns = k_stages_fit(bsum, g.pitch16max);
+    if (ns >= (G == 1 ? 2 : 3)) {
       g.G = G;
       g.bsum = bsum;
+      g.nstages = ns;
+      const size_t bytes = k_smem_bytes(bsum, g.pitch16max, ns);
       g.smem = bytes < 116 * 1024 ? 116 * 1024 : bytes;  // never two CTAs (2 x 512 TMEM columns) per SM
       return g;
     }
@@ -115,6 +118,7 @@ KGeom k_geometry(const starkv_layout& l) {
   g.bsum = 0;
   g.smem = 0;
   g.rmax = 0;
+  g.nstages = 0;
   return g;
 }
 
@@ -269,6 +273,8 @@ int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp
   if (rc) return rc;
   if (!a || !a->q || !a->k_u || !a->k_cache || !a->inv_freq) return set_error(STARKV_ERR_INVALID, "null argument");
   if (lay->quantized && !a->k_scales) return set_error(STARKV_ERR_INVALID, "quantised layout needs k_scales");
+  if (reinterpret_cast<uintptr_t>(a->k_cache) % 16)
+    return set_error(STARKV_ERR_INVALID, "k_cache must be 16-byte aligned");
   if (a->num_tokens <= 0 || a->num_tokens > lay->capacity)
     return set_error(STARKV_ERR_INVALID, "num_tokens outside (0, capacity]");
   rc = check_device();
@@ -287,6 +293,7 @@ int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp
   kp.rmax = g.rmax;
   kp.bsum = g.bsum;
   kp.pitch16max = g.pitch16max;
+  kp.nstages = g.nstages;
   kp.inv_freq = a->inv_freq;
   kp.trace = g_trace;
   kp.trace_jobs = g_trace_jobs;
@@ -425,7 +432,7 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   const int tiles_per = (ntiles + ns - 1) / ns;
   kp.mask = a->mask;
   kp.logits = reinterpret_cast<float*>(ws + w.logits);
-  kp.stats = reinterpret_cast<float2*>(ws + w.stats);
+  kp.smax = reinterpret_cast<float*>(ws + w.stats);     // split maxima, then split sums (same region)
   kp.err = reinterpret_cast<int*>(ws + w.err);
   kp.nsplit = ns;
   kp.tps = tiles_per * 128;
@@ -442,7 +449,8 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   memset(&vp, 0, sizeof(vp));
   vp.lay = *lay;
   vp.logits = kp.logits;
-  vp.stats = kp.stats;
+  vp.smax = kp.smax;
+  vp.lsum = kp.smax + (size_t)lay->batch * lay->num_q_heads * ns;
   vp.v_cache = a->v_cache;
   vp.v_params = reinterpret_cast<const __half2*>(a->v_params);
   vp.partial = reinterpret_cast<float*>(ws + w.partial);
@@ -460,6 +468,7 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   memset(&cp, 0, sizeof(cp));
   cp.lay = *lay;
   cp.partial = vp.partial;
+  cp.lsum = vp.lsum;
   cp.v_u = a->v_u;
   cp.out = a->out;
   cp.w_dtype = a->w_dtype;

@@ -16,7 +16,8 @@ namespace starkv {
 struct VParams {
   starkv_layout lay;
   const float* logits;   // (B, Hq, T) log2-domain logits (decode) ...
-  const float2* stats;   // (B, Hq, nsplit_k) split (max, sum exp2)
+  const float* smax;     // (B, Hq, nsplit_k) maximum logit of each K split
+  float* lsum;           // (B, Hq, nsplit) sum of exp2(logit - max) over each split (decode)
   const float* probs;    // ... or (B, Hq, T) probabilities (bx mode) when non-null
   const void* v_cache;
   const __half2* v_params;
@@ -108,7 +109,6 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 64);
   volatile int* s_fail = reinterpret_cast<volatile int*>(smem + 68);
   float* s_mx = reinterpret_cast<float*>(smem + 256);             // [32]
-  float* s_il = reinterpret_cast<float*>(smem + 384);             // [32]
   uint8_t* Abuf = smem + kVHeader;                                 // [2][kVABytes]
   uint8_t* Bbuf = Abuf + 2 * kVABytes;                             // [2][kVBBytes]
 
@@ -127,17 +127,11 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
   }
   for (int gw = warp; !p.probs && gw < Gv; gw += kVThreads / 32) {
     const int qh = qh0 + gw;
-    float m = kNegBig, l = 0.f;
-    for (int s = lane; s < p.nsplit_k; s += 32) {
-      const float2 st = p.stats[((int64_t)b * Hq + qh) * p.nsplit_k + s];
-      softmax_merge(m, l, st.x, st.y);
-    }
+    float m = kNegBig;
+    for (int s = lane; s < p.nsplit_k; s += 32) m = fmaxf(m, p.smax[((int64_t)b * Hq + qh) * p.nsplit_k + s]);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), l2 = __shfl_xor_sync(0xffffffffu, l, o);
-      softmax_merge(m, l, m2, l2);
-    }
-    if (lane == 0) { s_mx[gw] = m; s_il[gw] = l > 0.f ? kVPScale / l : 0.f; }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) s_mx[gw] = m;
   }
   fence_proxy_async_smem();
   tc_fence_before();
@@ -155,6 +149,7 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
   uint4 cw[kMaxItems][CW];
   __half2 sz[kMaxItems];
   float lg[8];
+  float psum = 0.f;      // this thread's share of sum exp2(logit - max) (decode)
 
   auto load_tile = [&](int t) {
     const int t0 = t_begin + t * kVTile;
@@ -219,7 +214,15 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
         float pv = 0.f;
-        if (l0 + e < t_end) pv = p.probs ? lg[e] * kVPScale : exp2f(lg[e] - s_mx[g]) * s_il[g];
+        if (l0 + e < t_end) {
+          if (p.probs) {
+            pv = lg[e] * kVPScale;
+          } else {
+            const float x = exp2f(lg[e] - s_mx[g]);
+            psum += x;
+            pv = x * kVPScale;
+          }
+        }
         h[e] = __float2half_rn(pv);
       }
       *reinterpret_cast<uint4*>(Bm + (g >> 3) * 1024 + kb * 128 + (g & 7) * 16) = *reinterpret_cast<uint4*>(h);
@@ -250,6 +253,13 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
                      smem_desc(b0 + ks * 256, 128, 1024), IDESC, (t > 0 || ks > 0) ? 1u : 0u);
       mma_commit(mma_bar + buf);
     }
+  }
+  // ---- split sums of the exponentials (threads 8g .. 8g+7 hold head g; channel tile 0 writes)
+  if (!p.probs && !*s_fail) {
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+    if (ct == 0 && tid < 8 * Gv && (tid & 7) == 0)
+      p.lsum[((int64_t)b * Hq + qh0 + (tid >> 3)) * p.nsplit + split] = psum;
   }
   // ---- wait for the last MMAs, read D[c, g] and write the partials
   if (tid == 0 && ntiles > 0 && !*s_fail) {
@@ -297,6 +307,7 @@ __global__ void __launch_bounds__(kVThreads) v_latent_kernel(const __grid_consta
 struct CombineParams {
   starkv_layout lay;
   const float* partial;
+  const float* lsum;     // (B, Hq, nsplit) split sums of the softmax exponentials
   const void* v_u;
   void* out;
   int w_dtype, out_dtype, nsplit, rv_max;
@@ -310,11 +321,21 @@ __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ Co
   int blk = 0;
   while (blk + 1 < lay.num_v_blocks && lay.v_first_kv[blk + 1] <= kv) ++blk;
   const int r = lay.v_rank[blk], vcol = lay.v_col[blk], R = lay.v_rank_total;
+  __shared__ float s_inv;
+  if (tid < 32) {
+    float L = 0.f;
+    for (int k = tid; k < p.nsplit; k += 32) L += p.lsum[((int64_t)b * Hq + qh) * p.nsplit + k];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (tid == 0) s_inv = L > 0.f ? 1.f / L : 0.f;
+  }
+  __syncthreads();
+  const float inv = s_inv;
   for (int c = tid; c < r; c += 128) {
     float s = 0.f;
     const float* src = p.partial + ((int64_t)b * Hq + qh) * p.nsplit * p.rv_max + c;
     for (int k = 0; k < p.nsplit; ++k) s += src[(int64_t)k * p.rv_max];
-    o_lat[c] = s;
+    o_lat[c] = s * inv;
   }
   __syncthreads();
   const int64_t urow = ((int64_t)kv * 128 + tid) * R + vcol;
