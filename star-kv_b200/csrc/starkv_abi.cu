@@ -53,10 +53,12 @@ int device_sm_count(int* dev_out) {
 // Raise a kernel's dynamic shared-memory limit once per (kernel, device).
 template <typename K>
 int ensure_smem(K kernel, size_t bytes, int slot) {
-  static size_t configured[16][kMaxDevices] = {{0}};
+  constexpr int kSlots = 24;
+  static size_t configured[kSlots][kMaxDevices] = {{0}};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= kMaxDevices || slot < 0 || slot >= 16) return STARKV_ERR_INVALID;
+  if (dev < 0 || dev >= kMaxDevices || slot < 0 || slot >= kSlots)
+    return set_error(STARKV_ERR_INVALID, "internal: kernel attribute slot out of range");
   if (configured[slot][dev] >= bytes) return STARKV_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
     return fail_launch();
@@ -143,18 +145,69 @@ int auto_splits(const starkv_layout& l, int T, int sms) {
   return best;
 }
 
+// Streaming V kernel (int4 latents, all V blocks per CTA): applicability and shared memory.
+struct V2Geom {
+  bool ok;
+  int np, nstages, stage_bytes, b_bytes;
+  size_t smem;
+};
+
+V2Geom v2_geometry(const starkv_layout& l) {
+  V2Geom g;
+  memset(&g, 0, sizeof(g));
+  if (!l.quantized) return g;
+  const int Hq = l.num_q_heads, qpk = Hq / l.num_kv_heads, R = l.v_rank_total;
+  if (Hq > kV2MaxHeads || Hq % 8) return g;
+  int gmax = 0, units = 0;
+  for (int j = 0; j < l.num_v_blocks; ++j) {
+    gmax = l.v_num_kv[j] * qpk > gmax ? l.v_num_kv[j] * qpk : gmax;
+    units += (l.v_rank[j] + 127) / 128;
+  }
+  g.np = gmax <= 16 ? 16 : 32;
+  if (gmax > 32 || units > kV2MaxUnits || units * g.np > 512) return g;
+  g.stage_bytes = v2_stage_bytes(R);
+  g.b_bytes = l.num_v_blocks * g.np * 128;
+  const long fixed = (long)kV2Header + (long)kV2Abufs * kV2ABytes + 2L * g.b_bytes;
+  long ns = (227L * 1024 - fixed) / g.stage_bytes;
+  if (ns > kV2MaxStages) ns = kV2MaxStages;
+  if (ns < 2) return g;
+  g.nstages = (int)ns;
+  g.smem = v2_smem_bytes(g.nstages, g.stage_bytes, g.b_bytes);
+  if (g.smem < 116 * 1024) g.smem = 116 * 1024;                 // one CTA per SM (512 TMEM columns)
+  g.ok = true;
+  return g;
+}
+
+// V splits of the streaming kernel: one CTA per SM over (split, sequence), at
+// least two 64-token tiles per split.
+int v2_splits(const starkv_layout& l, int T, int sms) {
+  int ns = (sms > 0 ? sms : 148) / l.batch;
+  const int cap = (T + 2 * kV2Tile - 1) / (2 * kV2Tile);
+  if (ns > cap) ns = cap;
+  return ns < 1 ? 1 : ns;
+}
+
+// Splits of the V pass: the streaming kernel's own, else the K splits.
+int v_splits(const starkv_layout& l, int T, int ns_k, int sms) {
+  return v2_geometry(l).ok ? v2_splits(l, T, sms) : ns_k;
+}
+
 struct WsLayout {
   size_t err, logits, stats, partial, total;
 };
 
-WsLayout ws_layout(const starkv_layout& l, int T, int ns) {
+// stats: K split maxima (B, Hq, ns_k), then V split sums (B, Hq, nsv); partial (B, Hq, nsv, rv_max).
+// nsv covers both V kernels (the streaming one may fall back at run time).
+WsLayout ws_layout(const starkv_layout& l, int T, int ns_k, int sms) {
   WsLayout w;
   const size_t BH = (size_t)l.batch * l.num_q_heads;
+  const int v2 = v_splits(l, T, ns_k, sms);
+  const size_t nsv = (size_t)(v2 > ns_k ? v2 : ns_k);
   w.err = 0;
   w.logits = 256;
   w.stats = w.logits + align256(BH * T * sizeof(float));
-  w.partial = w.stats + align256(BH * ns * sizeof(float2));
-  w.total = w.partial + align256(BH * ns * max_v_rank(l) * sizeof(float));
+  w.partial = w.stats + align256(BH * (ns_k + nsv) * sizeof(float));
+  w.total = w.partial + align256(BH * nsv * max_v_rank(l) * sizeof(float));
   return w;
 }
 
@@ -258,6 +311,15 @@ int launch_v(const VParams& vp, int nsplit, cudaStream_t st) {
   return fail_launch();
 }
 
+template <int NP>
+int launch_v2(const V2Params& p, const V2Geom& g, cudaStream_t st) {
+  auto kern = v_decode_kernel<NP>;
+  int rc = ensure_smem(kern, g.smem, NP == 16 ? 16 : 17);
+  if (rc) return rc;
+  kern<<<dim3(p.nsplit, p.lay.batch), kV2Threads, g.smem, st>>>(p);
+  return fail_launch();
+}
+
 int dispatch_v(const VParams& vp, int nsplit, cudaStream_t st) {
   if (vp.lay.quantized) return launch_v<uint8_t, true>(vp, nsplit, st);
   switch (vp.lay.latent_dtype) {
@@ -321,7 +383,8 @@ int starkv_decode_workspace_size(const starkv_layout* lay, int32_t num_tokens, i
   if (rc) return rc;
   if (!bytes || num_tokens <= 0) return set_error(STARKV_ERR_INVALID, "bad arguments");
   const int ns = num_splits > 0 ? num_splits : starkv_auto_splits(lay, num_tokens);
-  *bytes = ws_layout(*lay, num_tokens, ns).total;
+  const int sms = device_sm_count(nullptr);
+  *bytes = ws_layout(*lay, num_tokens, ns, sms > 0 ? sms : 148).total;
   return STARKV_OK;
 }
 
@@ -423,7 +486,7 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   const int T = a->num_tokens;
   const int sms = device_sm_count(nullptr);
   const int ns = a->num_splits > 0 ? a->num_splits : auto_splits(*lay, T, sms);
-  const WsLayout w = ws_layout(*lay, T, ns);
+  const WsLayout w = ws_layout(*lay, T, ns, sms);
   if (a->workspace_bytes < w.total) return set_error(STARKV_ERR_WORKSPACE, "workspace too small");
   cudaStream_t st = (cudaStream_t)stream;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
@@ -445,36 +508,70 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   if (rc) return rc;
   if (ev) cudaEventRecord(ev[1], st);
 
-  VParams vp;
-  memset(&vp, 0, sizeof(vp));
-  vp.lay = *lay;
-  vp.logits = kp.logits;
-  vp.smax = kp.smax;
-  vp.lsum = kp.smax + (size_t)lay->batch * lay->num_q_heads * ns;
-  vp.v_cache = a->v_cache;
-  vp.v_params = reinterpret_cast<const __half2*>(a->v_params);
-  vp.partial = reinterpret_cast<float*>(ws + w.partial);
-  vp.T = T;
-  vp.nsplit = ns;
-  vp.nsplit_k = ns;
-  vp.tps = kp.tps;
-  vp.rv_max = max_v_rank(*lay);
-  vp.err = kp.err;
-  rc = dispatch_v(vp, ns, st);
+  if (lay->quantized &&
+      (reinterpret_cast<uintptr_t>(a->v_cache) % 16 || reinterpret_cast<uintptr_t>(a->v_params) % 16))
+    return set_error(STARKV_ERR_INVALID, "v_cache and v_params must be 16-byte aligned");
+  const V2Geom vg = v2_geometry(*lay);
+  const bool stream_v = vg.ok;
+  const int nsv = stream_v ? v2_splits(*lay, T, sms) : ns;
+  float* lsum = kp.smax + (size_t)lay->batch * lay->num_q_heads * ns;
+  float* partial = reinterpret_cast<float*>(ws + w.partial);
+  if (stream_v) {
+    V2Params v2;
+    memset(&v2, 0, sizeof(v2));
+    v2.lay = *lay;
+    v2.logits = kp.logits;
+    v2.smax = kp.smax;
+    v2.lsum = lsum;
+    v2.v_cache = reinterpret_cast<const uint8_t*>(a->v_cache);
+    v2.v_params = reinterpret_cast<const uint8_t*>(a->v_params);
+    v2.partial = partial;
+    v2.err = kp.err;
+    v2.T = T;
+    v2.nsplit = nsv;
+    v2.nsplit_k = ns;
+    v2.tps = ((T + nsv * kV2Tile - 1) / (nsv * kV2Tile)) * kV2Tile;
+    v2.rv_max = max_v_rank(*lay);
+    v2.nstages = vg.nstages;
+    v2.stage_bytes = vg.stage_bytes;
+    v2.b_bytes = vg.b_bytes;
+    if (g_trace) {                                 // after the K timeline (2 traced CTAs)
+      v2.trace = g_trace + (size_t)2 * g_trace_jobs * kTrFields;
+      v2.trace_tiles = g_trace_jobs;
+    }
+    rc = vg.np == 16 ? launch_v2<16>(v2, vg, st) : launch_v2<32>(v2, vg, st);
+  } else {
+    VParams vp;
+    memset(&vp, 0, sizeof(vp));
+    vp.lay = *lay;
+    vp.logits = kp.logits;
+    vp.smax = kp.smax;
+    vp.lsum = lsum;
+    vp.v_cache = a->v_cache;
+    vp.v_params = reinterpret_cast<const __half2*>(a->v_params);
+    vp.partial = partial;
+    vp.T = T;
+    vp.nsplit = ns;
+    vp.nsplit_k = ns;
+    vp.tps = kp.tps;
+    vp.rv_max = max_v_rank(*lay);
+    vp.err = kp.err;
+    rc = dispatch_v(vp, ns, st);
+  }
   if (rc) return rc;
   if (ev) cudaEventRecord(ev[2], st);
 
   CombineParams cp;
   memset(&cp, 0, sizeof(cp));
   cp.lay = *lay;
-  cp.partial = vp.partial;
-  cp.lsum = vp.lsum;
+  cp.partial = partial;
+  cp.lsum = lsum;
   cp.v_u = a->v_u;
   cp.out = a->out;
   cp.w_dtype = a->w_dtype;
   cp.out_dtype = a->out_dtype;
-  cp.nsplit = ns;
-  cp.rv_max = vp.rv_max;
+  cp.nsplit = nsv;
+  cp.rv_max = max_v_rank(*lay);
   combine_kernel<<<dim3(lay->num_q_heads, lay->batch), 128, 0, st>>>(cp);
   rc = fail_launch();
   if (!rc && ev) cudaEventRecord(ev[3], st);
@@ -597,7 +694,7 @@ int starkv_decode_attention_static(const starkv_layout* lay, const starkv_decode
   const int sms = device_sm_count(nullptr);
   if (sms < 0) return set_error(STARKV_ERR_LAUNCH, "no CUDA device");
   const int ns = args->num_splits > 0 ? args->num_splits : auto_splits(*lay, args->num_tokens, sms);
-  const size_t need = ws_layout(*lay, args->num_tokens, ns).total;
+  const size_t need = ws_layout(*lay, args->num_tokens, ns, sms).total;
   if (need > kStaticScratchBytes) {
     char msg[200];
     snprintf(msg, sizeof(msg),

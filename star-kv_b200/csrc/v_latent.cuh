@@ -344,4 +344,387 @@ __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ Co
   store_from_f32(p.out, p.out_dtype, ((int64_t)b * Hq + qh) * 128 + tid, acc);
 }
 
+// ============================================================================
+// Decode V path, streaming form (int4 latents): CTA = (V split, sequence b), all
+// V blocks and all query heads of the layer, one CTA per SM.
+//
+// A 64-token tile of one sequence is one contiguous block of int4 codes
+// (64 x R/2 bytes) and one of fp16 (scale, zero) pairs (64 x R/8 bytes) in HBM:
+//   producer warp:  1-D bulk copies of both into a ring of shared-memory stages;
+//   dequant warps (8, four pairs): per (V block, 128-channel M tile) "M unit",
+//                   q*s + z (one fp16 rounding) into one of 4 MN-major A tiles (128
+//                   channels x 64 tokens); pair p owns A tile p, so four M units
+//                   are converted at once;
+//   prob warps (2): p = exp2(logit - M_h) for every head (M_h = maximum over the
+//                   K splits), fp16(p * 2^12) into per-block K-major B tiles
+//                   (double-buffered by tile), and the running sum of p;
+//   MMA thread:     4 tcgen05.mma (M=128, N=NP, K=16) per M unit and tile into
+//                   the M unit's accumulator D[channel, head] in TMEM.
+// At the end the dequant warps read the accumulators and write the split
+// partials; the prob warps write the split sums of p.  The combine kernel
+// divides by the total sum.
+// ============================================================================
+constexpr int kV2Threads = 384;
+constexpr int kV2Tile = 64;
+constexpr int kV2Abufs = 4;
+constexpr int kV2ABytes = 16384;     // 128 channels x 64 tokens fp16
+constexpr int kV2Header = 2048;
+constexpr int kV2MaxStages = 4;
+constexpr int kV2MaxUnits = 64;
+constexpr int kV2MaxHeads = 64;
+
+struct V2Params {
+  starkv_layout lay;
+  const float* logits;   // (B, Hq, T) log2-domain logits
+  const float* smax;     // (B, Hq, nsplit_k) maximum logit of each K split
+  float* lsum;           // (B, Hq, nsplit) sum of exp2(logit - max) over each V split
+  const uint8_t* v_cache;
+  const uint8_t* v_params;
+  float* partial;        // (B, Hq, nsplit, rv_max)
+  int* err;
+  int T, nsplit, nsplit_k, tps, rv_max;
+  int nstages, stage_bytes, b_bytes;
+  long long* trace;      // optional per-tile clock64 timeline of CTA (0, 0); null = off
+  int trace_tiles;
+};
+
+enum V2Trace { kV2TrIssue = 0, kV2TrStage, kV2TrDequant, kV2TrProbs, kV2TrMmaB, kV2TrMmaDone, kV2TrFields = 8 };
+
+__host__ __device__ inline int v2_stage_bytes(int R) {
+  return ((kV2Tile * (R / 2) + kV2Tile * (R / 8) + 16) + 127) & ~127;
+}
+__host__ __device__ inline size_t v2_smem_bytes(int nstages, int stage_bytes, int b_bytes) {
+  return (size_t)kV2Header + (size_t)nstages * stage_bytes + (size_t)kV2Abufs * kV2ABytes + 2 * (size_t)b_bytes;
+}
+
+// 8 int4 codes (4 bytes, even channel in the low nibble) -> 8 fp16 of q*s + z.
+__device__ __forceinline__ uint4 dequant8_i4(uint32_t w, __half2 s2, __half2 z2) {
+  const __half2 k1024 = __half2half2(__ushort_as_half((unsigned short)0x6400));
+  const uint32_t x = w & 0x0F0F0F0Fu, y = (w >> 4) & 0x0F0F0F0Fu;
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t v = __byte_perm(x, y, (uint32_t)(i | ((4 + i) << 8)));
+    v = (v & 0x000F000Fu) | 0x64006400u;
+    __half2 h = __hsub2(*reinterpret_cast<__half2*>(&v), k1024);
+    h = __hfma2(h, s2, z2);
+    o[i] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <int NP>
+__global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_constant__ V2Params p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const starkv_layout& lay = p.lay;
+  const int split = blockIdx.x, b = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Hq = lay.num_q_heads, qpk = Hq / lay.num_kv_heads;
+  const int R = lay.v_rank_total;
+  const int t_begin = split * p.tps, t_end = min(p.T, t_begin + p.tps);
+  const int ntiles = t_end > t_begin ? (t_end - t_begin + kV2Tile - 1) / kV2Tile : 0;
+  const int NS = p.nstages;
+  const int code_row = R / 2, par_row = R / 8;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* st_full = bars;            // [4]
+  uint64_t* st_empty = bars + 4;       // [4]  8 dequant warps
+  uint64_t* a_full = bars + 8;         // [4]  the slot's dequant warp pair
+  uint64_t* a_empty = bars + 12;       // [4]  commit
+  uint64_t* b_full = bars + 16;        // [2]  2 prob warps
+  uint64_t* b_empty = bars + 18;       // [2]  commit
+  uint64_t* fin_bar = bars + 20;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 192);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 196);
+  int* s_nunits = reinterpret_cast<int*>(smem + 200);
+  uint8_t* s_ublk = smem + 256;                               // [64] V block of M unit m
+  uint8_t* s_umt = smem + 320;                                // [64] M tile of M unit m
+  int* s_boffB = reinterpret_cast<int*>(smem + 384);          // [32] B tile offset of V block
+  float* s_mx = reinterpret_cast<float*>(smem + 512);         // [64] softmax maximum per head
+  float* s_ps = reinterpret_cast<float*>(smem + 768);         // [2][64] prob-warp sums
+  uint8_t* Ssm = smem + kV2Header;
+  uint8_t* Asm = Ssm + (size_t)NS * p.stage_bytes;
+  uint8_t* Bsm = Asm + (size_t)kV2Abufs * kV2ABytes;
+
+  if (tid == 0) {
+    for (int k = 0; k < kV2MaxStages; ++k) {
+      mbar_init(st_full + k, 1);
+      mbar_init(st_empty + k, 8);
+    }
+    for (int k = 0; k < kV2Abufs; ++k) {
+      mbar_init(a_full + k, 2);        // the slot's warp pair
+      mbar_init(a_empty + k, 1);
+    }
+    for (int k = 0; k < 2; ++k) {
+      mbar_init(b_full + k, 2);
+      mbar_init(b_empty + k, 1);
+    }
+    mbar_init(fin_bar, 1);
+    *s_abort = 0;
+    int m = 0;
+    for (int j = 0; j < lay.num_v_blocks; ++j) {
+      s_boffB[j] = j * NP * 128;
+      for (int mt = 0; mt * 128 < lay.v_rank[j]; ++mt, ++m) {
+        s_ublk[m] = (uint8_t)j;
+        s_umt[m] = (uint8_t)mt;
+      }
+    }
+    *s_nunits = m;
+    fence_mbar_init();
+  }
+  // zero the B tiles once: padded heads stay zero
+  for (int e = tid; e < (2 * p.b_bytes) / 16; e += kV2Threads) reinterpret_cast<uint4*>(Bsm)[e] = make_uint4(0u, 0u, 0u, 0u);
+  if (warp == 0) {                     // one CTA per SM: all 512 columns
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int MU = *s_nunits;
+  auto fail = [&](int code) {
+    record_error(p.err, code);
+    *s_abort = 1;
+  };
+  long long* trace = (p.trace && split == 0 && b == 0) ? p.trace : nullptr;
+  auto stamp = [&](int t, int f) {
+    if (trace && t < p.trace_tiles) trace[(int64_t)t * kV2TrFields + f] = clock64();
+  };
+  long long* mtrace = trace ? trace + (int64_t)p.trace_tiles * kV2TrFields : nullptr;   // per M unit: 4 fields
+
+  if (warp == 0) {
+    // ============================================================ producer
+    if (lane == 0) {
+      int issued = 0;
+      for (int t = 0; t < ntiles; ++t, issued = t) {
+        if (*s_abort) break;
+        const int s = t % NS;
+        if (!mbar_wait(st_empty + s, (uint32_t)(((t / NS) & 1) ^ 1))) { fail(kDevWaitCopy); break; }
+        stamp(t, kV2TrIssue);
+        const int t0 = t_begin + t * kV2Tile;
+        const int nrows = min(kV2Tile, t_end - t0);
+        const int64_t row0 = (int64_t)b * lay.capacity + t0;
+        const uint32_t cb = (uint32_t)(nrows * code_row);
+        // parameters: the 16-byte-aligned span inside [row0, row0 + nrows) rows;
+        // the unaligned tail is read from global by the dequant warps
+        const int64_t pstart = row0 * par_row, pa = pstart & ~(int64_t)15;
+        const int64_t pend = (pstart + (int64_t)nrows * par_row) & ~(int64_t)15;
+        const uint32_t pb = pend > pa ? (uint32_t)(pend - pa) : 0u;
+        mbar_arrive_expect_tx(st_full + s, cb + pb);
+        uint8_t* dst = Ssm + (size_t)s * p.stage_bytes;
+        bulk_g2s(dst, p.v_cache + row0 * code_row, cb, st_full + s);
+        if (pb) bulk_g2s(dst + kV2Tile * code_row, p.v_params + pa, pb, st_full + s);
+      }
+      for (int t = max(0, issued - NS); t < issued; ++t)
+        if (!mbar_wait(st_full + (t % NS), (uint32_t)((t / NS) & 1))) { fail(kDevWaitCopy); break; }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC = (1u << 4) | (1u << 15) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+      int mc = 0;
+      bool ok = true;
+      for (int t = 0; t < ntiles && ok; ++t) {
+        if (*s_abort) break;
+        const int tb = t & 1;
+        if (!mbar_wait(b_full + tb, (uint32_t)((t >> 1) & 1))) { ok = false; break; }
+        stamp(t, kV2TrMmaB);
+        const uint32_t bt = smem_u32(Bsm + tb * p.b_bytes);
+        for (int m = 0; m < MU; ++m, ++mc) {
+          const int k = mc & (kV2Abufs - 1);
+          if (!mbar_wait(a_full + k, (uint32_t)((mc / kV2Abufs) & 1))) { ok = false; break; }
+          tc_fence_after();
+          if (mtrace && mc < p.trace_tiles) mtrace[mc * 4 + 2] = clock64();
+          const uint64_t ad = smem_desc(smem_u32(Asm + k * kV2ABytes), 128, 1024);
+          const uint64_t bd = smem_desc(bt + (uint32_t)s_boffB[s_ublk[m]], 128, 1024);
+          const uint32_t d = tmem + (uint32_t)(m * NP);
+#pragma unroll
+          for (int ks = 0; ks < kV2Tile / 16; ++ks)
+            mma_f16_ss(d, ad + (uint64_t)(ks * 16), bd + (uint64_t)(ks * 16), IDESC, (t > 0 || ks > 0) ? 1u : 0u);
+          mma_commit(a_empty + k);
+          if (mtrace && mc < p.trace_tiles) mtrace[mc * 4 + 3] = clock64();
+        }
+        mma_commit(b_empty + tb);
+        stamp(t, kV2TrMmaDone);
+      }
+      if (!ok) fail(kDevWaitMma);
+      mma_commit(fin_bar);
+      if (!mbar_wait(fin_bar, 0)) fail(kDevWaitMma);
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    // ============================================================ prob warps
+    const int pw = warp - 2, pt = tid - 64;
+    for (int h = pt; h < Hq; h += 64) {
+      float m = kNegBig;
+      for (int s = 0; s < p.nsplit_k; ++s) m = fmaxf(m, p.smax[((int64_t)b * Hq + h) * p.nsplit_k + s]);
+      s_mx[h] = m;
+    }
+    named_bar_sync(1, 64);
+    const int G8 = Hq >> 3;
+    // destination of this lane's (head, 8-token block) in a B tile, per head group
+    int dstoff[kV2MaxHeads / 8];
+    float mh[kV2MaxHeads / 8], psum[kV2MaxHeads / 8];
+#pragma unroll
+    for (int q = 0; q < kV2MaxHeads / 8; ++q) {
+      dstoff[q] = 0;
+      mh[q] = 0.f;
+      psum[q] = 0.f;
+      if (q < G8) {
+        const int g = q * 8 + (lane & 7), kv = g / qpk;
+        int blk = 0;
+        while (blk + 1 < lay.num_v_blocks && lay.v_first_kv[blk + 1] <= kv) ++blk;
+        const int gl = g - lay.v_first_kv[blk] * qpk;
+        dstoff[q] = s_boffB[blk] + (gl >> 3) * 1024 + (gl & 7) * 16;
+        mh[q] = s_mx[g];
+      }
+    }
+    const int kb = (lane >> 3) + 4 * pw;           // 8-token block of the tile
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) {
+      if (*s_abort) break;
+      const int tb = t & 1;
+      const int l0 = t_begin + t * kV2Tile + kb * 8;
+      float lg[kV2MaxHeads / 8][8];
+#pragma unroll
+      for (int q = 0; q < kV2MaxHeads / 8; ++q)
+        if (q < G8) {
+          const float* src = p.logits + ((int64_t)b * Hq + q * 8 + (lane & 7)) * p.T + l0;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) lg[q][e] = (l0 + e < t_end) ? src[e] : kNegBig;
+        }
+      if (!mbar_wait(b_empty + tb, (uint32_t)(((t >> 1) & 1) ^ 1))) { ok = false; break; }
+      uint8_t* Bt = Bsm + tb * p.b_bytes + kb * 128;
+#pragma unroll
+      for (int q = 0; q < kV2MaxHeads / 8; ++q)
+        if (q < G8) {
+          __align__(16) __half hv[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float x = (l0 + e < t_end) ? exp2f(lg[q][e] - mh[q]) : 0.f;
+            psum[q] += x;
+            hv[e] = __float2half_rn(x * kVPScale);
+          }
+          *reinterpret_cast<uint4*>(Bt + dstoff[q]) = *reinterpret_cast<uint4*>(hv);
+        }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(b_full + tb);
+      if (tid == 64) stamp(t, kV2TrProbs);
+    }
+    if (!ok) fail(kDevWaitMma);
+    // sum over the 4 lanes of a head (same lane & 7), then over the two warps
+#pragma unroll
+    for (int q = 0; q < kV2MaxHeads / 8; ++q) {
+      float v = psum[q];
+      v += __shfl_xor_sync(0xffffffffu, v, 8);
+      v += __shfl_xor_sync(0xffffffffu, v, 16);
+      if (q < G8 && lane < 8) s_ps[pw * 64 + q * 8 + lane] = v;
+    }
+    named_bar_sync(1, 64);
+    if (!*s_abort)
+      for (int h = pt; h < Hq; h += 64) p.lsum[((int64_t)b * Hq + h) * p.nsplit + split] = s_ps[h] + s_ps[64 + h];
+  } else {
+    // ============================================================ dequant warps
+    // Four warp pairs: pair p fills A slot p with the M units whose running
+    // index mc = t * MU + m is p mod 4, so four M units are in flight.
+    const int dw = warp - 4;                       // 0..7
+    const int pair = dw >> 1, pl = (dw & 1) * 32 + lane;
+    int mc = 0;
+    bool ok = true;
+    for (int t = 0; t < ntiles && ok; ++t) {
+      if (*s_abort) break;
+      const int s = t % NS;
+      if (!mbar_wait(st_full + s, (uint32_t)((t / NS) & 1))) { ok = false; break; }
+      if (tid == 128) stamp(t, kV2TrStage);
+      const uint8_t* codes = Ssm + (size_t)s * p.stage_bytes;
+      const uint8_t* pars = codes + kV2Tile * code_row;
+      const int t0 = t_begin + t * kV2Tile;
+      const int nrows = min(kV2Tile, t_end - t0);
+      const int64_t pstart = ((int64_t)b * lay.capacity + t0) * par_row;
+      const int pdelta = (int)(pstart & 15);                // stage byte of parameter row 0
+      const int64_t pend = (pstart + (int64_t)nrows * par_row) & ~(int64_t)15;
+      const int pcopied = pend > (pstart & ~(int64_t)15) ? (int)(pend - (pstart & ~(int64_t)15)) : 0;
+      const uint8_t* gpars = p.v_params + pstart;
+      for (int m = 0; m < MU; ++m, ++mc) {
+        const int k = mc & (kV2Abufs - 1);
+        if (k != pair) continue;
+        if (!mbar_wait(a_empty + k, (uint32_t)(((mc / kV2Abufs) & 1) ^ 1))) { ok = false; break; }
+        if (mtrace && mc < p.trace_tiles && pl == 0) mtrace[mc * 4 + 0] = clock64();
+        const int blk = s_ublk[m], mt = s_umt[m];
+        const int c0 = lay.v_col[blk] + mt * 128;            // first global channel of the M tile
+        const int nch = min(128, lay.v_rank[blk] - mt * 128);
+        const int gc = nch >> 5;                             // 32-channel groups in the M tile
+        uint8_t* A = Asm + k * kV2ABytes;
+        // item = (token, 32-channel group); 8 consecutive lanes = 8 tokens of one
+        // group, so every 16-byte store phase covers 128 contiguous bytes
+#pragma unroll 2
+        for (int it = pl; it < gc * kV2Tile; it += 64) {
+          const int grp = (it >> 3) % gc, l = ((it >> 3) / gc) * 8 + (it & 7);
+          uint4 o[4] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u),
+                        make_uint4(0u, 0u, 0u, 0u)};
+          if (l < nrows) {
+            const uint4 w = *reinterpret_cast<const uint4*>(codes + l * code_row + (c0 >> 1) + grp * 16);
+            const int po = l * par_row + ((c0 >> 5) + grp) * 4;
+            const uint32_t pz = pdelta + po + 4 <= pcopied ? *reinterpret_cast<const uint32_t*>(pars + pdelta + po)
+                                                           : *reinterpret_cast<const uint32_t*>(gpars + po);
+            const __half2 sz = *reinterpret_cast<const __half2*>(&pz);
+#ifdef V2_NODQ
+            o[0] = w; o[1] = w; o[2] = w; o[3] = make_uint4(pz, 0u, 0u, 0u);
+            (void)sz;
+#else
+            dequant32_i4(w, __half2half2(__low2half(sz)), __half2half2(__high2half(sz)), o);
+#endif
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            *reinterpret_cast<uint4*>(A + (grp * 4 + u) * 1024 + (l >> 3) * 128 + (l & 7) * 16) = o[u];
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(a_full + k);
+        if (mtrace && mc < p.trace_tiles && pl == 0) mtrace[mc * 4 + 1] = clock64();
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(st_empty + s);
+      if (tid == 128) stamp(t, kV2TrDequant);
+    }
+    if (!ok) fail(kDevWaitMma);
+    // ---- epilogue: accumulators -> split partials (warp quarter = TMEM lanes)
+    const bool have = ntiles > 0 && !*s_abort;
+    if (have && !mbar_wait(fin_bar, 0)) fail(kDevWaitMma);
+    tc_fence_after();
+    const int q4 = warp & 3;
+    for (int m = dw >> 2; m < MU; m += 2) {
+      const int blk = s_ublk[m], mt = s_umt[m];
+      const int Gv = lay.v_num_kv[blk] * qpk, qh0 = lay.v_first_kv[blk] * qpk;
+      float d[NP];
+      const uint32_t ta = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(m * NP);
+      if (have && !*s_abort) {
+        if constexpr (NP == 16) tmem_ld16(ta, d);
+        else tmem_ld32(ta, d);
+      } else {
+#pragma unroll
+        for (int g = 0; g < NP; ++g) d[g] = 0.f;
+      }
+      const int c = mt * 128 + q4 * 32 + lane;               // channel within the V block
+      if (c < lay.v_rank[blk]) {
+#pragma unroll
+        for (int g = 0; g < NP; ++g)
+          if (g < Gv)
+            p.partial[(((int64_t)b * Hq + qh0 + g) * p.nsplit + split) * p.rv_max + c] = d[g] * (1.f / kVPScale);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace starkv
