@@ -309,7 +309,7 @@ def main():
     v_bytes = rank_bytes - k_bytes
     k_gbs = k_bytes / (k_ms / 1e3) / 1e9
     traffic = ncu_traffic()
-    roofline = {"kernel": "k_logits_kernel<int8_t,true> (fused K reconstruction + RoPE + q.k + split softmax)",
+    roofline = {"kernel": "k_logits_kernel<int8_t,true,G> (fused K reconstruction + RoPE + q.k, split maxima)",
                 "bound": "hbm", "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak,
                 "peak_kind": peak_kind,
                 "traffic": (traffic or {}).get("dram_bytes_per_launch_full_size"),
