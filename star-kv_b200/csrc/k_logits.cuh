@@ -509,28 +509,49 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       regs_dec<kKConvRegs>();
       const int ct = tid - 128;                          // token row = TMEM lane
       const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+      // Unit u's TMEM stores complete (and it is handed to the MMA issuer) after the
+      // next unit's waits, so the store latency overlaps them.
+      int s = 0, sph = 0, n = 0, t = 0;            // stage, its phase, run, tile of unit u
+      int prev_s = -1, prev_a = -1, prev_j = 0;
+      bool ok = true;
       for (int u = 0; u < U; ++u) {
-        if (*s_abort) break;
-        const int s = u % NS, a = u & (kKAbufs - 1);
-        const int t = u / NR, n = u - t * NR;
+        if (*s_abort) { ok = false; break; }
+        const int a = u & (kKAbufs - 1);
         const int g0 = s_run0[n], r = s_rank[g0];
         const int j = t * G + g0;
-        if (!mbar_wait(st_full + s, (uint32_t)((u / NS) & 1))) { fail(kDevWaitCopy); break; }
+        if (!mbar_wait(st_full + s, (uint32_t)sph)) { fail(kDevWaitCopy); ok = false; break; }
         if (ct == 0) stamp(j, kTrConvBegin);
-        if (!mbar_wait(a_empty + a, (uint32_t)(((u / kKAbufs) & 1) ^ 1))) { fail(kDevWaitMma); break; }
+        if (!mbar_wait(a_empty + a, (uint32_t)(((u >> 2) & 1) ^ 1))) { fail(kDevWaitMma); ok = false; break; }
         tc_fence_after();
         if (ct == 0) stamp(j, kTrConvAEmpty);
         const int rc = (r * XB) >> 4;
         const uint8_t* srow = Ssm + (size_t)s * stage_bytes + (size_t)ct * r * XB;
+        if (prev_a >= 0) {                         // hand over the previous unit
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            mbar_arrive(st_empty + prev_s);
+            mbar_arrive(a_full + prev_a);
+          }
+          if (ct == 0) stamp(prev_j, kTrConvDone);
+        }
         convert_row<XT>(rc, srow, lane_base + 256u + (uint32_t)a * 64u);
+        prev_s = s;
+        prev_a = a;
+        prev_j = j;
+        if (++s == NS) { s = 0; sph ^= 1; }
+        if (++n == NR) { n = 0; ++t; }
+      }
+      if (ok && prev_a >= 0) {
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(st_empty + s);
-          mbar_arrive(a_full + a);
+          mbar_arrive(st_empty + prev_s);
+          mbar_arrive(a_full + prev_a);
         }
-        if (ct == 0) stamp(j, kTrConvDone);
+        if (ct == 0) stamp(prev_j, kTrConvDone);
       }
     } else {
       // ============================================================ drain: frequency half h
