@@ -325,7 +325,7 @@ def main():
         "kernels_ms": {"k_logits": k_ms, "v_latent": v_ms, "combine": c_ms},
         "v_kernel_gbs": v_bytes / (v_ms / 1e3) / 1e9,
         "roofline": roofline,
-        "gpu_launches": 5 * K,
+        "gpu_launches": 6 * K,                    # append (2), W pre-pass, K, V, combine
         "e2e": e2e,
         "clocks": clk.summary(),
     }

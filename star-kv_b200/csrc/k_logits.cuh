@@ -72,6 +72,9 @@ struct KParams {
   int nstages;            // staging ring depth
   float out_scale;        // multiplier of q.k (scaling * log2 e for decode)
   float mask_scale;       // multiplier of the mask (log2 e for decode)
+  const uint8_t* wpre;    // W of every (sequence, query head) from k_wprep_kernel (stride wstride), or null:
+  const float* weta;      //   then the CTA builds its W itself; eta of every (sequence, query head)
+  int wstride;            // bytes per (sequence, query head) W image
   long long* trace;       // optional per-job clock64 timeline of CTAs (0, 0, b < 2); null = off
   int trace_jobs;         // jobs recorded per traced CTA
 };
@@ -207,12 +210,95 @@ __device__ __forceinline__ void exact_sincos(int l, float w, float& c, float& s)
   __sincosf((float)red, &s, &c);
 }
 
+// Build W_h = [P | Q] of query head qh for sequence b (fp16, canonical no-swizzle
+// K-major layout: row n of W^T, n < 64 -> P, else Q) into Bg, by NT threads
+// (thread index t); red holds NT / 32 floats; bar() synchronises the NT threads.
+// One pass: thread chunk e = (row i, channels 8kc..8kc+7) computes 8 P and 8 Q
+// entries (kc fastest: coalesced U rows), then the block maximum sets the
+// power-of-two normalisation eta (largest entries in [2^13, 2^14], fp16's full
+// precision; undone in the drain), then fp16 stores.
+template <bool QUANT, int NT, typename Bar>
+__device__ __forceinline__ void build_w_head(const KParams& p, int b, int qh, const float* qv, uint8_t* Bg, float* red,
+                                             int t, Bar bar, float& eta) {
+  const starkv_layout& lay = p.lay;
+  const int kv = qh / (lay.num_q_heads / lay.num_kv_heads), r = lay.k_rank[kv];
+  const int64_t ubase = (int64_t)128 * lay.k_col[kv];
+  const __half* scp = QUANT ? p.k_scales + (int64_t)b * lay.k_rank_total + lay.k_col[kv] : nullptr;
+  const int nc = r >> 3, nch = 64 * nc;
+  constexpr int kPer = (64 * (STARKV_MAX_K_RANK / 8) + NT - 1) / NT;
+  float pv[kPer][8], qq[kPer][8];
+  float amax = 0.f;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int e = t + NT * k;
+    if (e < nch) {
+      const int i = e / nc, kc = e - i * nc;
+      const float qa = qv[i], qb = qv[i + 64];
+#pragma unroll
+      for (int cc = 0; cc < 8; ++cc) {
+        const int c = kc * 8 + cc;
+        const float u1 = load_as_f32(p.k_u, p.w_dtype, ubase + (int64_t)i * r + c);
+        const float u2 = load_as_f32(p.k_u, p.w_dtype, ubase + (int64_t)(i + 64) * r + c);
+        const float sc = QUANT ? __half2float(scp[c]) : 1.f;
+        pv[k][cc] = sc * (qa * u1 + qb * u2);
+        qq[k][cc] = sc * (qb * u1 - qa * u2);
+        amax = fmaxf(amax, fmaxf(fabsf(pv[k][cc]), fabsf(qq[k][cc])));
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  if ((t & 31) == 0) red[t >> 5] = amax;
+  bar();
+  amax = 0.f;
+  for (int w = 0; w < NT / 32; ++w) amax = fmaxf(amax, red[w]);
+  bar();                                                   // red is reused by the caller
+  eta = amax > 0.f ? exp2f(ceilf(log2f(amax)) - 14.f) : 1.f;
+  const float inv_eta = 1.f / eta;
+#pragma unroll
+  for (int k = 0; k < kPer; ++k) {
+    const int e = t + NT * k;
+    if (e < nch) {
+      const int i = e / nc, kc = e - i * nc;
+      uint32_t op[4], oq[4];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        __half2 hp = __floats2half2_rn(pv[k][2 * m] * inv_eta, pv[k][2 * m + 1] * inv_eta);
+        __half2 hq = __floats2half2_rn(qq[k][2 * m] * inv_eta, qq[k][2 * m + 1] * inv_eta);
+        op[m] = *reinterpret_cast<uint32_t*>(&hp);
+        oq[m] = *reinterpret_cast<uint32_t*>(&hq);
+      }
+      *reinterpret_cast<uint4*>(Bg + (i >> 3) * (r * 16) + kc * 128 + (i & 7) * 16) = make_uint4(op[0], op[1], op[2], op[3]);
+      *reinterpret_cast<uint4*>(Bg + ((64 + i) >> 3) * (r * 16) + kc * 128 + (i & 7) * 16) = make_uint4(oq[0], oq[1], oq[2], oq[3]);
+    }
+  }
+}
+
+// Pre-pass: W and eta of every (sequence, query head) into the workspace, so that
+// the K kernel's prologue is a bulk copy.  grid (Hq, B), 256 threads.
+template <bool QUANT>
+__global__ void __launch_bounds__(256) k_wprep_kernel(const __grid_constant__ KParams p, uint8_t* wout, float* eout) {
+  __shared__ float qv[128];
+  __shared__ float red[8];
+  const int qh = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+  const int Hq = p.lay.num_q_heads;
+  if (t < 128) qv[t] = load_as_f32(p.q, p.q_dtype, ((int64_t)b * Hq + qh) * 128 + t);
+  __syncthreads();
+  float eta;
+  build_w_head<QUANT, 256>(p, b, qh, qv, wout + ((int64_t)b * Hq + qh) * p.wstride, red, t, [] { __syncthreads(); }, eta);
+  if (t == 0) eout[(int64_t)b * Hq + qh] = eta;
+}
+
 template <typename XT, bool QUANT, int G>
 __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_constant__ KParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int wg = warp >> 2;                      // warpgroup 0..3
   const int split = blockIdx.x, grp = blockIdx.y, b = blockIdx.z;
+#ifdef KTRACE_CTA
+  const unsigned long long t_start = global_timer_ns();
+  __shared__ unsigned long long w_done_s;
+#endif
   const starkv_layout& lay = p.lay;
   const int Hq = lay.num_q_heads, qpk = Hq / lay.num_kv_heads;
   const int t_begin = split * p.tps;
@@ -232,6 +318,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   uint64_t* fin_bar = bars + 28;
   uint64_t* part_full = bars + 29;               // [8]  both halves' partials stored (8 drain warps)
   uint64_t* part_empty = bars + 37;              // [8]  slot read by the job's finaliser warp
+  uint64_t* w_bar = bars + 45;                   // W images landed (pre-pass mode)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 512);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 516);
   int* s_nruns = reinterpret_cast<int*>(smem + 520);
@@ -263,6 +350,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       mbar_init(d_empty + k, 8);       // both drain warpgroups
     }
     mbar_init(fin_bar, 1);
+    mbar_init(w_bar, 1);
     for (int k = 0; k < kKPartRing; ++k) {
       mbar_init(part_full + k, 8);     // both drain warpgroups
       mbar_init(part_empty + k, 1);    // the finaliser warp of the job
@@ -311,6 +399,14 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
     regs_dec<kKCtlRegs>();
     if (warp == 0) {
       // ============================================================ producer warp
+      if (p.wpre && lane == 0) {
+        uint32_t wb = 0;
+        for (int g = 0; g < G; ++g) wb += (uint32_t)s_rank[g] * 256u;
+        mbar_arrive_expect_tx(w_bar, wb);
+        for (int g = 0; g < G; ++g)
+          bulk_g2s(Bsm + s_boff[g], p.wpre + ((int64_t)b * Hq + grp * G + g) * p.wstride, (uint32_t)s_rank[g] * 256u, w_bar);
+      }
+      __syncwarp();
       int issued = 0;
       for (int u = 0; u < U; ++u, issued = u) {
         if (*s_abort) break;
@@ -336,6 +432,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
     } else if (warp == 1) {
       // ============================================================ MMA issuer
       named_bar_sync(1, 416 + 64);               // W matrices built (builders + this warp + finalisers)
+      if (p.wpre && lane == 0 && !mbar_wait(w_bar, 0)) fail(kDevWaitCopy);
       if (lane == 0) {
         constexpr uint32_t IDESC = idesc_f16_f32(128, 128);
         // Per-head operands in registers (G is a compile-time constant, so every
@@ -431,76 +528,29 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
     // ---- build W_g = [P | Q] (fp16, canonical K-major layout) for each head: 384 threads
     {
       const int bt = tid - 128;
-      for (int e = bt; e < G * 128; e += 384)
-        s_qall[e] = load_as_f32(p.q, p.q_dtype, ((int64_t)b * Hq + grp * G) * 128 + e);
+      if (p.wpre) {                                    // W came from the pre-pass (bulk-copied by the producer)
+        if (bt < G) s_epi[bt] = p.weta[(int64_t)b * Hq + grp * G + bt] * p.out_scale;
+      } else {
+        for (int e = bt; e < G * 128; e += 384)
+          s_qall[e] = load_as_f32(p.q, p.q_dtype, ((int64_t)b * Hq + grp * G) * 128 + e);
+      }
       if (bt < 64) {
         float c, sn;
         exact_sincos(128, p.inv_freq[bt], c, sn);
         s_rot[bt] = make_float2(c, sn);
       }
       named_bar_sync(2, 384);
-      for (int g = 0; g < G; ++g) {
-        const int qh = grp * G + g, kv = qh / qpk, r = lay.k_rank[kv];
+      for (int g = 0; g < G && !p.wpre; ++g) {
+        const int qh = grp * G + g;
         const float* qv = s_qall + g * 128;
-        const int64_t ubase = (int64_t)128 * lay.k_col[kv];
-        const __half* scp = QUANT ? p.k_scales + (int64_t)b * lay.k_rank_total + lay.k_col[kv] : nullptr;
-        // One pass: thread chunk e = (row i, channels 8kc..8kc+7) computes the 8 P and
-        // 8 Q entries (kc fastest: coalesced U rows), then the block maximum, then fp16.
-        const int nc = r >> 3, nch = 64 * nc;
-        constexpr int kPer = 3;                           // 64 * 16 chunks / 384 threads, rounded up
-        float pv[kPer][8], qq[kPer][8];
-        float amax = 0.f;
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-          const int e = bt + 384 * k;
-          if (e < nch) {
-            const int i = e / nc, kc = e - i * nc;
-            const float qa = qv[i], qb = qv[i + 64];
-#pragma unroll
-            for (int cc = 0; cc < 8; ++cc) {
-              const int c = kc * 8 + cc;
-              const float u1 = load_as_f32(p.k_u, p.w_dtype, ubase + (int64_t)i * r + c);
-              const float u2 = load_as_f32(p.k_u, p.w_dtype, ubase + (int64_t)(i + 64) * r + c);
-              const float sc = QUANT ? __half2float(scp[c]) : 1.f;
-              pv[k][cc] = sc * (qa * u1 + qb * u2);
-              qq[k][cc] = sc * (qb * u1 - qa * u2);
-              amax = fmaxf(amax, fmaxf(fabsf(pv[k][cc]), fabsf(qq[k][cc])));
-            }
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        if (lane == 0) s_red[warp - 4] = amax;
-        named_bar_sync(2, 384);
-        amax = 0.f;
-        for (int w = 0; w < 12; ++w) amax = fmaxf(amax, s_red[w]);
-        named_bar_sync(2, 384);                          // s_red is reused
-        // Power-of-two normalisation: the largest entries of W land in [2^13, 2^14],
-        // keeping fp16's full precision; undone exactly in the drain.
-        const float eta = amax > 0.f ? exp2f(ceilf(log2f(amax)) - 14.f) : 1.f;
-        const float inv_eta = 1.f / eta;
+        float eta;
+        build_w_head<QUANT, 384>(p, b, qh, qv, Bsm + s_boff[g], s_red, bt, [] { named_bar_sync(2, 384); }, eta);
         if (bt == 0) s_epi[g] = eta * p.out_scale;
-        uint8_t* Bg = Bsm + s_boff[g];
-#pragma unroll
-        for (int k = 0; k < kPer; ++k) {
-          const int e = bt + 384 * k;
-          if (e < nch) {
-            const int i = e / nc, kc = e - i * nc;
-            uint32_t op[4], oq[4];
-#pragma unroll
-            for (int m = 0; m < 4; ++m) {
-              __half2 hp = __floats2half2_rn(pv[k][2 * m] * inv_eta, pv[k][2 * m + 1] * inv_eta);
-              __half2 hq = __floats2half2_rn(qq[k][2 * m] * inv_eta, qq[k][2 * m + 1] * inv_eta);
-              op[m] = *reinterpret_cast<uint32_t*>(&hp);
-              oq[m] = *reinterpret_cast<uint32_t*>(&hq);
-            }
-            // row n of W^T (n = i for P, 64 + i for Q) in the canonical K-major layout
-            *reinterpret_cast<uint4*>(Bg + (i >> 3) * (r * 16) + kc * 128 + (i & 7) * 16) = make_uint4(op[0], op[1], op[2], op[3]);
-            *reinterpret_cast<uint4*>(Bg + ((64 + i) >> 3) * (r * 16) + kc * 128 + (i & 7) * 16) = make_uint4(oq[0], oq[1], oq[2], oq[3]);
-          }
-        }
       }
       fence_proxy_async_smem();
+#ifdef KTRACE_CTA
+      if (tid == 128) w_done_s = global_timer_ns();
+#endif
       named_bar_sync(1, 416 + 64);                       // W ready for the MMA warp (s_epi for the finalisers, s_rot for the drains)
     }
 
@@ -525,7 +575,11 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         tc_fence_after();
         if (ct == 0) stamp(j, kTrConvAEmpty);
         const int rc = (r * XB) >> 4;
+#ifdef KCONV_PADREAD
+        const uint8_t* srow = Ssm + (size_t)s * stage_bytes + (size_t)ct * k_pitch16(r, XB) * 16;
+#else
         const uint8_t* srow = Ssm + (size_t)s * stage_bytes + (size_t)ct * r * XB;
+#endif
         if (prev_a >= 0) {                         // hand over the previous unit
           tmem_st_wait();
           tc_fence_before();
@@ -614,6 +668,9 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   // every copy landed: the producer waited the last stages)
   tc_fence_before();
   __syncthreads();
+#ifdef KTRACE_CTA
+  const unsigned long long w_done = w_done_s;
+#endif
   if (p.smax && tid < G && !*s_abort) {
     const float M = fmaxf(s_red[tid * 8], s_red[tid * 8 + 1]);
     p.smax[((int64_t)b * Hq + grp * G + tid) * p.nsplit + split] = M;
@@ -622,6 +679,18 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+#ifdef KTRACE_CTA
+  if (tid == 0 && p.trace) {
+    long long* ct = p.trace + 2 * p.trace_jobs * kTrFields + 4096 * 8;   // after the V timeline
+    const int cid = (b * gridDim.y + grp) * gridDim.x + split;
+    ct[cid * 4 + 0] = (long long)t_start;
+    ct[cid * 4 + 1] = (long long)global_timer_ns();
+    ct[cid * 4 + 2] = (long long)w_done;
+    int sm;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+    ct[cid * 4 + 3] = sm;
+  }
+#endif
 }
 
 }  // namespace starkv

@@ -193,7 +193,7 @@ int v_splits(const starkv_layout& l, int T, int ns_k, int sms) {
 }
 
 struct WsLayout {
-  size_t err, logits, stats, partial, total;
+  size_t err, logits, stats, partial, wimg, weta, total;
 };
 
 // stats: K split maxima (B, Hq, ns_k), then V split sums (B, Hq, nsv); partial (B, Hq, nsv, rv_max).
@@ -207,7 +207,9 @@ WsLayout ws_layout(const starkv_layout& l, int T, int ns_k, int sms) {
   w.logits = 256;
   w.stats = w.logits + align256(BH * T * sizeof(float));
   w.partial = w.stats + align256(BH * (ns_k + nsv) * sizeof(float));
-  w.total = w.partial + align256(BH * nsv * max_v_rank(l) * sizeof(float));
+  w.wimg = w.partial + align256(BH * nsv * max_v_rank(l) * sizeof(float));
+  w.weta = w.wimg + align256(BH * (size_t)max_k_rank(l) * 256);
+  w.total = w.weta + align256(BH * sizeof(float));
   return w;
 }
 
@@ -495,6 +497,10 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   const int tiles_per = (ntiles + ns - 1) / ns;
   kp.mask = a->mask;
   kp.logits = reinterpret_cast<float*>(ws + w.logits);
+  // W of every (sequence, query head) once, ahead of the K kernel (its CTAs bulk-copy theirs)
+  kp.wstride = max_k_rank(*lay) * 256;
+  kp.wpre = ws + w.wimg;
+  kp.weta = reinterpret_cast<float*>(ws + w.weta);
   kp.smax = reinterpret_cast<float*>(ws + w.stats);     // split maxima, then split sums (same region)
   kp.err = reinterpret_cast<int*>(ws + w.err);
   kp.nsplit = ns;
@@ -504,6 +510,15 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   kp.mask_scale = log2e;
   cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(a->events);
   if (ev) cudaEventRecord(ev[0], st);
+  {
+    const dim3 wg(lay->num_q_heads, lay->batch);
+    if (lay->quantized)
+      k_wprep_kernel<true><<<wg, 256, 0, st>>>(kp, ws + w.wimg, reinterpret_cast<float*>(ws + w.weta));
+    else
+      k_wprep_kernel<false><<<wg, 256, 0, st>>>(kp, ws + w.wimg, reinterpret_cast<float*>(ws + w.weta));
+    rc = fail_launch();
+    if (rc) return rc;
+  }
   rc = dispatch_k(kp, g, st);
   if (rc) return rc;
   if (ev) cudaEventRecord(ev[1], st);
