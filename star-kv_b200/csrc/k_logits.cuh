@@ -68,8 +68,7 @@ struct KParams {
   int q_dtype, w_dtype;
   int T, nsplit, tps;     // tokens, splits, tokens per split (multiple of 128)
   int G, rmax, bsum;      // heads per CTA, max rank, max per-group rank sum (W matrices in smem)
-  int pitch16max;         // largest staging row pitch (16-byte units) over the heads
-  int nstages;            // staging ring depth
+  int stage_total;        // bytes of the staging ring
   float out_scale;        // multiplier of q.k (scaling * log2 e for decode)
   float mask_scale;       // multiplier of the mask (log2 e for decode)
   const uint8_t* wpre;    // W of every (sequence, query head) from k_wprep_kernel (stride wstride), or null:
@@ -82,39 +81,27 @@ struct KParams {
 // Per-job timeline fields (clock64 of the SM).
 enum KTrace {
   kTrLoadIssue = 0, kTrConvBegin, kTrConvAEmpty, kTrConvDone, kTrMmaIssue, kTrDrainWait, kTrDrainGot,
-  kTrDrainDone, kTrDrainLd, kTrFields = 10
+  kTrDrainDone, kTrDrainLd, kTrConvPre, kTrFields = 10
 };
 
-constexpr int kKThreads = 512;
-// Register budget per warpgroup after setmaxnreg: producer/MMA, converter, 2 drains.
-constexpr int kKCtlRegs = 56, kKConvRegs = 120, kKDrainRegs = 168;  // 56 + 120 + 2*168 = 4 * 128 (launch budget)
-constexpr int kKMaxStages = 8;   // staging ring depth (bounded by shared memory)
-constexpr int kKAbufs = 4;       // A buffers in TMEM
-constexpr int kKAcc = 2;         // accumulators in TMEM
-constexpr int kKPartRing = 8;    // partial-logit slots between the two drain warpgroups
+constexpr int kKThreads = 640;
+// Register budget per warpgroup after setmaxnreg: control, two converters, two
+// drains (40 + 2*56 + 2*160 = 472 <= 5 * 96, the launch budget).
+constexpr int kKCtlRegs = 40, kKConvRegs = 56, kKDrainRegs = 160;
+constexpr int kKAbufs = 2;       // A buffers in TMEM (columns [384, 512)), one per converter warpgroup
+constexpr int kKAcc = 3;         // accumulators in TMEM (columns [0, 384))
 constexpr int kKHeader = 12288;  // barriers / scratch / partial-logit ring at the start of dynamic smem
 constexpr int kKSmemMax = 227 * 1024;
 
-// Staging row pitch in 16-byte units.  Rows whose chunk count is a multiple of 4
-// would put 4+ rows of a quarter-warp on the same banks: they get one chunk of
-// padding; other counts conflict at most 2-way and stay unpadded.
-__host__ __device__ inline int k_pitch16(int r, int xbytes) {
-  const int rc = (r * xbytes) >> 4;
-  return (rc & 3) == 0 ? rc + 1 : rc;
-}
+// Staging ring: a CTA's units are staged row-major (one bulk copy of 128 * R
+// contiguous bytes, R = r * element size) into tile slots; a tile slot holds the
+// units of every run of one 128-token tile back to back, and the ring has as
+// many tile slots as shared memory allows (at most kKMaxSlots unit slots).
+constexpr int kKMaxSlots = 32;
 
-__host__ __device__ inline size_t k_stage_bytes(int pitch16max) { return (size_t)128 * pitch16max * 16; }
-
-__host__ __device__ inline size_t k_smem_bytes(int bsum, int pitch16max, int nstages) {
-  return (size_t)kKHeader + (size_t)bsum * 256 + (size_t)nstages * k_stage_bytes(pitch16max);
-}
-
-// Staging depth that fits next to the W matrices (0 when fewer than 2 fit).
-__host__ __device__ inline int k_stages_fit(int bsum, int pitch16max) {
-  const long avail = (long)kKSmemMax - kKHeader - (long)bsum * 256;
-  long ns = avail > 0 ? avail / (long)k_stage_bytes(pitch16max) : 0;
-  if (ns > kKMaxStages) ns = kKMaxStages;
-  return ns >= 2 ? (int)ns : 0;
+// Staging bytes next to the W matrices of one CTA (one CTA per SM).
+__host__ __device__ inline long k_stage_total(int bsum) {
+  return ((long)kKSmemMax - kKHeader - (long)bsum * 256) & ~15L;
 }
 
 // 8 int8 codes -> 8 fp16 (exact): x -> (x + 128) as a byte; 0x64XX as fp16 is
@@ -176,26 +163,70 @@ template <typename XT, int N>
 __device__ __forceinline__ void convert_chunks(const uint8_t* srow, uint32_t taddr) {
   uint4 w[N];
 #pragma unroll
-  for (int c = 0; c < N; ++c) w[c] = *reinterpret_cast<const uint4*>(srow + c * 16);
+  for (int c = 0; c < N; ++c) w[c] = *reinterpret_cast<const uint4*>(srow + 16 * c);
 #pragma unroll
   for (int c = 0; c < N; ++c) cvt_store<XT>(w[c], taddr + c * k_cols_per_chunk<XT>());
 }
 
-// Convert a staged row of rc chunks into TMEM: groups of 8 chunks, then the rest.
+// int8 row of RC chunks: loads, conversions into registers, then the fewest wide
+// TMEM stores (x32 / x16 / x8 columns), at most 4 chunks (32 columns) at a time.
+template <int N>
+__device__ __forceinline__ void convert_row_i8(const uint8_t* srow, uint32_t taddr) {
+  if constexpr (N > 4) {
+    convert_row_i8<4>(srow, taddr);
+    convert_row_i8<N - 4>(srow + 64, taddr + 32);
+  } else {
+    uint4 w[N];
+#pragma unroll
+    for (int c = 0; c < N; ++c) w[c] = *reinterpret_cast<const uint4*>(srow + 16 * c);
+    uint32_t o[8 * N];
+#pragma unroll
+    for (int c = 0; c < N; ++c) {
+      cvt8_i8(w[c].x, w[c].y, o + 8 * c);
+      cvt8_i8(w[c].z, w[c].w, o + 8 * c + 4);
+    }
+    if constexpr (N == 4) {
+      tmem_st32(taddr, o);
+    } else {
+      int col = 0;
+      if constexpr (N >= 2) {
+        tmem_st16(taddr, o);
+        col = 16;
+      }
+      if constexpr (N & 1) tmem_st8(taddr + col, o + col);
+    }
+  }
+}
+
+// Convert a staged row of rc chunks into TMEM: int8 rows in one piece, other
+// element types in groups of 8 chunks, then the rest.
 template <typename XT>
 __device__ __forceinline__ void convert_row(int rc, const uint8_t* srow, uint32_t taddr) {
+  if constexpr (sizeof(XT) == 1) {
+    switch (rc) {
+      case 1: convert_row_i8<1>(srow, taddr); return;
+      case 2: convert_row_i8<2>(srow, taddr); return;
+      case 3: convert_row_i8<3>(srow, taddr); return;
+      case 4: convert_row_i8<4>(srow, taddr); return;
+      case 5: convert_row_i8<5>(srow, taddr); return;
+      case 6: convert_row_i8<6>(srow, taddr); return;
+      case 7: convert_row_i8<7>(srow, taddr); return;
+      case 8: convert_row_i8<8>(srow, taddr); return;
+      default: break;
+    }
+  }
   int c = 0;
-  for (; c + 8 <= rc; c += 8) convert_chunks<XT, 8>(srow + c * 16, taddr + c * k_cols_per_chunk<XT>());
-  const uint8_t* s = srow + c * 16;
+  for (; c + 8 <= rc; c += 8) convert_chunks<XT, 8>(srow + 16 * c, taddr + c * k_cols_per_chunk<XT>());
+  const uint8_t* sr = srow + 16 * c;
   const uint32_t t = taddr + c * k_cols_per_chunk<XT>();
   switch (rc - c) {
-    case 1: convert_chunks<XT, 1>(s, t); break;
-    case 2: convert_chunks<XT, 2>(s, t); break;
-    case 3: convert_chunks<XT, 3>(s, t); break;
-    case 4: convert_chunks<XT, 4>(s, t); break;
-    case 5: convert_chunks<XT, 5>(s, t); break;
-    case 6: convert_chunks<XT, 6>(s, t); break;
-    case 7: convert_chunks<XT, 7>(s, t); break;
+    case 1: convert_chunks<XT, 1>(sr, t); break;
+    case 2: convert_chunks<XT, 2>(sr, t); break;
+    case 3: convert_chunks<XT, 3>(sr, t); break;
+    case 4: convert_chunks<XT, 4>(sr, t); break;
+    case 5: convert_chunks<XT, 5>(sr, t); break;
+    case 6: convert_chunks<XT, 6>(sr, t); break;
+    case 7: convert_chunks<XT, 7>(sr, t); break;
     default: break;
   }
 }
@@ -293,7 +324,7 @@ template <typename XT, bool QUANT, int G>
 __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_constant__ KParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int wg = warp >> 2;                      // warpgroup 0..3
+  const int wg = __shfl_sync(0xffffffffu, warp >> 2, 0);   // warpgroup 0..4 (warp-uniform)
   const int split = blockIdx.x, grp = blockIdx.y, b = blockIdx.z;
 #ifdef KTRACE_CTA
   const unsigned long long t_start = global_timer_ns();
@@ -304,40 +335,38 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   const int t_begin = split * p.tps;
   const int t_end = min(p.T, t_begin + p.tps);
   const int ntiles = t_end > t_begin ? (t_end - t_begin + 127) / 128 : 0;
-  const int NS = p.nstages;
   constexpr int XB = (int)sizeof(XT);
 
   // ---- shared memory carve-up
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* st_full = bars;                      // [8]  stage landed (tx bytes)
-  uint64_t* st_empty = bars + 8;                 // [8]  stage read by the 4 converter warps
-  uint64_t* a_full = bars + 16;                  // [4]  A buffer written (4 converter warps)
-  uint64_t* a_empty = bars + 20;                 // [4]  A buffer's MMAs retired (commit)
-  uint64_t* d_full = bars + 24;                  // [2]  accumulator ready (commit)
-  uint64_t* d_empty = bars + 26;                 // [2]  accumulator read by the 8 drain warps
-  uint64_t* fin_bar = bars + 28;
-  uint64_t* part_full = bars + 29;               // [8]  both halves' partials stored (8 drain warps)
-  uint64_t* part_empty = bars + 37;              // [8]  slot read by the job's finaliser warp
-  uint64_t* w_bar = bars + 45;                   // W images landed (pre-pass mode)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 8192);
+  uint64_t* st_full = bars;                      // [32] unit slot landed (tx bytes)
+  uint64_t* st_empty = bars + 32;                // [32] unit slot read by the 4 converter warps
+  uint64_t* a_full = bars + 64;                  // [2]  A buffer written (4 converter warps)
+  uint64_t* a_empty = bars + 80;                 // [2]  A buffer's MMAs retired (commit)
+  uint64_t* d_full = bars + 96;                  // [3]  accumulator ready (commit)
+  uint64_t* d_empty = bars + 99;                 // [3]  accumulator read by the job's 4 drain warps
+  uint64_t* fin_bar = bars + 102;
+  uint64_t* w_bar = bars + 103;                  // W images landed (pre-pass mode)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 512);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 516);
   int* s_nruns = reinterpret_cast<int*>(smem + 520);
   int* s_boff = reinterpret_cast<int*>(smem + 528);           // [4] byte offset of W_g
   int* s_rank = reinterpret_cast<int*>(smem + 544);           // [4] rank of head g
+  const uint8_t** s_src = reinterpret_cast<const uint8_t**>(smem + 640);  // [4] latents of (b, kv(g)) at slot 0
   float* s_epi = reinterpret_cast<float*>(smem + 560);        // [4]
   int* s_run0 = reinterpret_cast<int*>(smem + 576);           // [4] first head of run n
   int* s_runlen = reinterpret_cast<int*>(smem + 592);         // [4] heads in run n
-  const uint8_t** s_src = reinterpret_cast<const uint8_t**>(smem + 640);  // [4] latents of (b, kv(g)) at slot 0
   float* s_red = reinterpret_cast<float*>(smem + 704);        // [64]
   float2* s_rot = reinterpret_cast<float2*>(smem + 1024);     // [64] rotation by 128 positions
+  float4* s_rot4 = reinterpret_cast<float4*>(smem + 4096);    // [32] the same per frequency pair (cos.xy, sin.xy)
   float* s_qall = reinterpret_cast<float*>(smem + 1536);      // [4][128]
-  float* s_part = reinterpret_cast<float*>(smem + 4096);      // [8][2][128] partial logits of the two halves
   uint8_t* Bsm = smem + kKHeader;
   uint8_t* Ssm = Bsm + (size_t)p.bsum * 256;
-  const uint32_t stage_bytes = 128u * p.pitch16max * 16u;
+  int* s_runoff = reinterpret_cast<int*>(smem + 4608);        // [4] byte offset of run n in a tile slot
+  int* s_ring = reinterpret_cast<int*>(smem + 4624);          // [2] tile slots, bytes per tile slot
 
   if (tid == 0) {
-    for (int k = 0; k < kKMaxStages; ++k) {
+    for (int k = 0; k < kKMaxSlots; ++k) {
       mbar_init(st_full + k, 1);
       mbar_init(st_empty + k, 4);
     }
@@ -347,14 +376,10 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
     }
     for (int k = 0; k < kKAcc; ++k) {
       mbar_init(d_full + k, 1);
-      mbar_init(d_empty + k, 8);       // both drain warpgroups
+      mbar_init(d_empty + k, 4);       // the drain warpgroup of the job
     }
     mbar_init(fin_bar, 1);
     mbar_init(w_bar, 1);
-    for (int k = 0; k < kKPartRing; ++k) {
-      mbar_init(part_full + k, 8);     // both drain warpgroups
-      mbar_init(part_empty + k, 1);    // the finaliser warp of the job
-    }
     *s_abort = 0;
     int off = 0, nr = 0;
     for (int g = 0; g < G; ++g) {
@@ -371,6 +396,15 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       ++s_runlen[nr - 1];
     }
     *s_nruns = nr;
+    int tb = 0;
+    for (int n = 0; n < nr; ++n) {
+      s_runoff[n] = tb;
+      tb += 128 * s_rank[s_run0[n]] * XB;
+    }
+    int nt = p.stage_total / tb;
+    if (nt > kKMaxSlots / nr) nt = kKMaxSlots / nr;
+    s_ring[0] = nt;                              // >= 2 (checked on the host)
+    s_ring[1] = tb;
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -382,6 +416,8 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int NR = *s_nruns;
+  const int NT = s_ring[0];                      // tile slots in the ring
+  const int TB = s_ring[1];                      // bytes per tile slot
   const int U = ntiles * NR;                     // units of this CTA
   const int J = ntiles * G;                      // jobs of this CTA
 
@@ -408,30 +444,30 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       }
       __syncwarp();
       int issued = 0;
-      for (int u = 0; u < U; ++u, issued = u) {
-        if (*s_abort) break;
-        const int s = u % NS;
-        if (!mbar_wait(st_empty + s, (uint32_t)(((u / NS) & 1) ^ 1))) { fail(kDevWaitCopy); break; }
-        const int t = u / NR, n = u - t * NR;
-        const int g0 = s_run0[n], r = s_rank[g0];
-        const int t0 = t_begin + t * 128;
-        const int nrows = min(128, t_end - t0);
-        if (lane == 0) {
+      if (lane == 0) {
+        int t = 0, n = 0;                          // tile and run of unit u
+        for (int u = 0; u < U; ++u, issued = u) {
+          if (*s_abort) break;
+          const int ts = t % NT, slot = ts * NR + n;
+          if (!mbar_wait(st_empty + slot, (uint32_t)(((t / NT) & 1) ^ 1))) { fail(kDevWaitCopy); break; }
+          const int g0 = s_run0[n], R = s_rank[g0] * XB;
+          const int t0 = t_begin + t * 128;
+          const uint32_t bytes = (uint32_t)(min(128, t_end - t0) * R);
           stamp(t * G + g0, kTrLoadIssue);
-          const uint32_t bytes = (uint32_t)(nrows * r * XB);
-          mbar_arrive_expect_tx(st_full + s, bytes);
-          bulk_g2s(Ssm + (size_t)s * stage_bytes, s_src[g0] + (size_t)t0 * r * XB, bytes, st_full + s);
+          mbar_arrive_expect_tx(st_full + slot, bytes);
+          bulk_g2s(Ssm + (size_t)ts * TB + s_runoff[n], s_src[g0] + (size_t)t0 * R, bytes, st_full + slot);
+          if (++n == NR) { n = 0; ++t; }
         }
-        __syncwarp();
+        // every copy issued has landed before the CTA may exit
+        for (int u = max(0, issued - NT * NR); u < issued; ++u) {
+          const int tt = u / NR, slot = (tt % NT) * NR + (u - tt * NR);
+          if (!mbar_wait(st_full + slot, (uint32_t)((tt / NT) & 1))) { fail(kDevWaitCopy); break; }
+        }
       }
-      // every copy this warp issued has landed before the CTA may exit
-      if (lane == 0)
-        for (int u = max(0, issued - NS); u < issued; ++u)
-          if (!mbar_wait(st_full + (u % NS), (uint32_t)((u / NS) & 1))) { fail(kDevWaitCopy); break; }
       __syncwarp();
     } else if (warp == 1) {
       // ============================================================ MMA issuer
-      named_bar_sync(1, 416 + 64);               // W matrices built (builders + this warp + finalisers)
+      named_bar_sync(1, 512 + 96);               // W matrices built (builders + warps 1-3)
       if (p.wpre && lane == 0 && !mbar_wait(w_bar, 0)) fail(kDevWaitCopy);
       if (lane == 0) {
         constexpr uint32_t IDESC = idesc_f16_f32(128, 128);
@@ -450,24 +486,27 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         bool ok = true;
         int u = -1;                                // current unit
         uint32_t a_t = 0;
+        int db = 0;                                // accumulator of job j = j % kKAcc, and its phase
+        uint32_t dph = 0;
         for (int t = 0; t < ntiles && ok; ++t) {
           if (*s_abort) break;
 #pragma unroll
           for (int g = 0; g < G; ++g) {
-            const int j = t * G + g, db = j & 1;
+            const int j = t * G + g;
             if (first[g]) {
               ++u;
-              if (!mbar_wait(a_full + (u & (kKAbufs - 1)), (uint32_t)((u / kKAbufs) & 1))) { ok = false; break; }
-              a_t = tmem + 256u + (uint32_t)(u & (kKAbufs - 1)) * 64u;
+              if (!mbar_wait(a_full + (u & 1), (uint32_t)((u >> 1) & 1))) { ok = false; break; }
+              a_t = tmem + 384u + (uint32_t)(u & 1) * 64u;
             }
-            if (!mbar_wait(d_empty + db, (uint32_t)(((j >> 1) & 1) ^ 1))) { ok = false; break; }
+            if (!mbar_wait(d_empty + db, dph ^ 1u)) { ok = false; break; }
             tc_fence_after();
             stamp(j, kTrMmaIssue);
             const uint32_t d = tmem + (uint32_t)db * 128u;
             mma_f16_ts(d, a_t, bdesc[g], IDESC, 0u);
             for (int kk = 1; kk < nk[g]; ++kk) mma_f16_ts(d, a_t + kk * 8, bdesc[g] + (uint64_t)(kk * 16), IDESC, 1u);
             mma_commit(d_full + db);
-            if (g == G - 1 || first[(g + 1) % G]) mma_commit(a_empty + (u & (kKAbufs - 1)));
+            if (g == G - 1 || first[(g + 1) % G]) mma_commit(a_empty + (u & 1));
+            if (++db == kKAcc) { db = 0; dph ^= 1u; }
           }
         }
         if (!ok) fail(kDevWaitMma);
@@ -476,62 +515,17 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       }
       __syncwarp();
     } else {
-      // ============================================================ finaliser warps 2, 3
-      // Warp 2 + f finishes the jobs j with j % 2 == f: logit = (partial of the low
-      // frequencies + partial of the high ones) * scale (+ mask), written to global,
-      // and the running maximum per head.  Lane i covers rows i, i+32, i+64, i+96.
-      const int f = warp - 2;
-      named_bar_sync(1, 416 + 64);               // s_epi ready
-      float m_run[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) m_run[g] = kNegBig;
-      bool ok = true;
-      for (int j = f; j < J; j += 2) {
-        if (*s_abort) break;
-        const int pk = j % kKPartRing;
-        if (!mbar_wait(part_full + pk, (uint32_t)((j / kKPartRing) & 1))) { ok = false; break; }
-        float v[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) v[q] = s_part[pk * 256 + 32 * q + lane] + s_part[pk * 256 + 128 + 32 * q + lane];
-        __syncwarp();
-        if (lane == 0) mbar_arrive(part_empty + pk);
-        const int tile = j / G, g = j - tile * G;
-        const int l0 = t_begin + tile * 128 + lane;
-        const float sc = s_epi[g];
-        float* dst = p.logits + ((int64_t)b * Hq + grp * G + g) * p.T;
-        float mx = kNegBig;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int l = l0 + 32 * q;
-          if (l < t_end) {
-            float val = v[q] * sc;
-            if (p.mask) val = fmaf(p.mask[(int64_t)b * p.T + l], p.mask_scale, val);
-            dst[l] = val;
-            mx = fmaxf(mx, val);
-          }
-        }
-#pragma unroll
-        for (int gg = 0; gg < G; ++gg)
-          if (gg == g) m_run[gg] = fmaxf(m_run[gg], mx);
-        if (lane == 0) stamp(j, kTrDrainDone);
-      }
-      if (!ok) fail(kDevWaitMma);
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float m = m_run[g];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) s_red[g * 8 + f] = m;
-      }
+      // warps 2, 3: no role after the prologue barrier
+      named_bar_sync(1, 512 + 96);
     }
   } else {
-    // ---- build W_g = [P | Q] (fp16, canonical K-major layout) for each head: 384 threads
+    // ---- build W_g = [P | Q] (fp16, canonical K-major layout) for each head: 512 threads
     {
       const int bt = tid - 128;
       if (p.wpre) {                                    // W came from the pre-pass (bulk-copied by the producer)
         if (bt < G) s_epi[bt] = p.weta[(int64_t)b * Hq + grp * G + bt] * p.out_scale;
       } else {
-        for (int e = bt; e < G * 128; e += 384)
+        for (int e = bt; e < G * 128; e += 512)
           s_qall[e] = load_as_f32(p.q, p.q_dtype, ((int64_t)b * Hq + grp * G) * 128 + e);
       }
       if (bt < 64) {
@@ -539,128 +533,150 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         exact_sincos(128, p.inv_freq[bt], c, sn);
         s_rot[bt] = make_float2(c, sn);
       }
-      named_bar_sync(2, 384);
+      named_bar_sync(2, 512);
+      if (bt < 32)                                     // rotation of the pair (2bt, 2bt + 1): cos, sin, -sin
+        s_rot4[bt] = make_float4(s_rot[2 * bt].x, s_rot[2 * bt + 1].x, s_rot[2 * bt].y, s_rot[2 * bt + 1].y);
       for (int g = 0; g < G && !p.wpre; ++g) {
         const int qh = grp * G + g;
         const float* qv = s_qall + g * 128;
         float eta;
-        build_w_head<QUANT, 384>(p, b, qh, qv, Bsm + s_boff[g], s_red, bt, [] { named_bar_sync(2, 384); }, eta);
+        build_w_head<QUANT, 512>(p, b, qh, qv, Bsm + s_boff[g], s_red, bt, [] { named_bar_sync(2, 512); }, eta);
         if (bt == 0) s_epi[g] = eta * p.out_scale;
       }
       fence_proxy_async_smem();
 #ifdef KTRACE_CTA
       if (tid == 128) w_done_s = global_timer_ns();
 #endif
-      named_bar_sync(1, 416 + 64);                       // W ready for the MMA warp (s_epi for the finalisers, s_rot for the drains)
+      named_bar_sync(1, 512 + 96);                       // W ready for the MMA warp (s_epi, s_rot4 for the drains)
     }
 
-    if (wg == 1) {
-      // ============================================================ converter warpgroup
+    if (wg <= 2) {
+      // ============================================================ converter warpgroups
+      // Warpgroup c = wg - 1 converts the units u with u % 2 == c into A buffer c.
       regs_dec<kKConvRegs>();
-      const int ct = tid - 128;                          // token row = TMEM lane
+      const int cw = wg - 1;
+      const int ct = tid - 128 * wg;                     // token row = TMEM lane
       const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-      // Unit u's TMEM stores complete (and it is handed to the MMA issuer) after the
-      // next unit's waits, so the store latency overlaps them.
-      int s = 0, sph = 0, n = 0, t = 0;            // stage, its phase, run, tile of unit u
-      int prev_s = -1, prev_a = -1, prev_j = 0;
-      bool ok = true;
-      for (int u = 0; u < U; ++u) {
-        if (*s_abort) { ok = false; break; }
-        const int a = u & (kKAbufs - 1);
+      // Each unit is handed to the MMA issuer as soon as its TMEM stores complete
+      // (this warpgroup's next unit waits for the same A buffer to drain).
+      int n = cw, t = 0;                           // run, tile of unit u
+      while (n >= NR) { n -= NR; ++t; }
+      for (int u = cw; u < U; u += 2) {
+        if (*s_abort) break;
         const int g0 = s_run0[n], r = s_rank[g0];
         const int j = t * G + g0;
-        if (!mbar_wait(st_full + s, (uint32_t)sph)) { fail(kDevWaitCopy); ok = false; break; }
+        const int ts = t % NT, s = ts * NR + n;
+        if (!mbar_wait(st_full + s, (uint32_t)((t / NT) & 1))) { fail(kDevWaitCopy); break; }
         if (ct == 0) stamp(j, kTrConvBegin);
-        if (!mbar_wait(a_empty + a, (uint32_t)(((u >> 2) & 1) ^ 1))) { fail(kDevWaitMma); ok = false; break; }
+        if (!mbar_wait(a_empty + cw, (uint32_t)(((u >> 1) & 1) ^ 1))) { fail(kDevWaitMma); break; }
         tc_fence_after();
         if (ct == 0) stamp(j, kTrConvAEmpty);
         const int rc = (r * XB) >> 4;
-#ifdef KCONV_PADREAD
-        const uint8_t* srow = Ssm + (size_t)s * stage_bytes + (size_t)ct * k_pitch16(r, XB) * 16;
-#else
-        const uint8_t* srow = Ssm + (size_t)s * stage_bytes + (size_t)ct * r * XB;
-#endif
-        if (prev_a >= 0) {                         // hand over the previous unit
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(st_empty + prev_s);
-            mbar_arrive(a_full + prev_a);
-          }
-          if (ct == 0) stamp(prev_j, kTrConvDone);
-        }
-        convert_row<XT>(rc, srow, lane_base + 256u + (uint32_t)a * 64u);
-        prev_s = s;
-        prev_a = a;
-        prev_j = j;
-        if (++s == NS) { s = 0; sph ^= 1; }
-        if (++n == NR) { n = 0; ++t; }
-      }
-      if (ok && prev_a >= 0) {
+        const uint8_t* srow = Ssm + (size_t)ts * TB + s_runoff[n] + (size_t)ct * r * XB;
+        convert_row<XT>(rc, srow, lane_base + 384u + (uint32_t)cw * 64u);
+        if (ct == 0) stamp(j, kTrConvPre);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(st_empty + prev_s);
-          mbar_arrive(a_full + prev_a);
+          mbar_arrive(st_empty + s);
+          mbar_arrive(a_full + cw);
         }
-        if (ct == 0) stamp(prev_j, kTrConvDone);
+        if (ct == 0) stamp(j, kTrConvDone);
+        n += 2;
+        while (n >= NR) { n -= NR; ++t; }
       }
     } else {
-      // ============================================================ drain: frequency half h
+      // ============================================================ drain warpgroups
+      // Warpgroup w = wg - 3 takes the jobs j with j % 2 == w.  Per job: thread =
+      // token row (TMEM lane) with cos / sin of all 64 frequencies at its token in
+      // registers (advanced by 128 positions per tile with packed fp32x2
+      // rotations), eight 16-column TMEM loads, packed fp32x2 FMAs, then scale,
+      // mask, the logit to HBM and the running maximum per head.
       regs_inc<kKDrainRegs>();
-      const int h = wg - 2;
+      const int w2 = wg - 3;
       const int dw = warp & 3;                           // TMEM lane quarter
       const int row = dw * 32 + lane;
-      float2 cs_c[16], cs_s[16];                         // cos / sin of frequencies 32h + (2i, 2i+1)
+      float2 cs_c[32], cs_s[32];                         // cos / sin of frequencies (2i, 2i+1)
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        exact_sincos(t_begin + row, p.inv_freq[32 * h + 2 * i], cs_c[i].x, cs_s[i].x);
-        exact_sincos(t_begin + row, p.inv_freq[32 * h + 2 * i + 1], cs_c[i].y, cs_s[i].y);
+      for (int i = 0; i < 32; ++i) {
+        exact_sincos(t_begin + row, p.inv_freq[2 * i], cs_c[i].x, cs_s[i].x);
+        exact_sincos(t_begin + row, p.inv_freq[2 * i + 1], cs_c[i].y, cs_s[i].y);
       }
-      const uint32_t lbase = tmem + ((uint32_t)(dw * 32) << 16) + 32u * h;
-      bool ok = true;
-      int j = 0;
-      for (; j < J && ok; ++j) {
-        if (*s_abort) { ok = false; break; }
-        const int tile = j / G, g = j - tile * G, db = j & 1;
-        if (g == 0 && tile > 0) {                        // advance every frequency by 128 positions
+      int cur_tile = 0;
+      float m_run[G];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float2 r0 = s_rot[32 * h + 2 * i], r1 = s_rot[32 * h + 2 * i + 1];
+      for (int g = 0; g < G; ++g) m_run[g] = kNegBig;
+      const uint32_t lbase = tmem + ((uint32_t)(dw * 32) << 16);
+      float* const lg_base = p.logits + ((int64_t)b * Hq + grp * G) * p.T + t_begin + row;
+      bool ok = true;
+      int db = w2;                                       // accumulator of job j = j % kKAcc and its phase
+      uint32_t dph = 0;
+      for (int j = w2; j < J && ok; j += 2) {
+        if (*s_abort) { ok = false; break; }
+        const int tile = j / G, g = j - tile * G;
+        for (; cur_tile < tile; ++cur_tile) {            // advance every frequency by 128 positions
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float4 r = s_rot4[i];
+            const float2 rc = make_float2(r.x, r.y), rs = make_float2(r.z, r.w);
             const float2 c = cs_c[i], sn = cs_s[i];
-            cs_c[i] = make_float2(fmaf(c.x, r0.x, -sn.x * r0.y), fmaf(c.y, r1.x, -sn.y * r1.y));
-            cs_s[i] = make_float2(fmaf(sn.x, r0.x, c.x * r0.y), fmaf(sn.y, r1.x, c.y * r1.y));
+            const float2 u = __fmul2_rn(sn, rs), v = __fmul2_rn(c, rs);
+            cs_c[i] = __ffma2_rn(c, rc, make_float2(-u.x, -u.y));
+            cs_s[i] = __ffma2_rn(sn, rc, v);
+            asm volatile("" ::: "memory");               // keep each constant's load beside its use (no hoisting)
           }
         }
-        if (row == 0 && h == 0) stamp(j, kTrDrainWait);
-        if (!mbar_wait(d_full + db, (uint32_t)((j >> 1) & 1))) { ok = false; break; }
+        if (row == 0) stamp(j, kTrDrainWait);
+        if (!mbar_wait(d_full + db, dph)) { ok = false; break; }
         tc_fence_after();
-        if (row == 0 && h == 0) stamp(j, kTrDrainGot);
+        if (row == 0) stamp(j, kTrDrainGot);
         const uint32_t ta = lbase + (uint32_t)db * 128u;
-        float va[32], vc[32];
-        tmem_ld16x4(ta, ta + 16, ta + 64, ta + 80, va, va + 16, vc, vc + 16);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(d_empty + db);      // accumulator free for the MMA of job j + 2
-        if (row == 0 && h == 0) stamp(j, kTrDrainLd);
-        float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+        float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          acc[0] = __ffma2_rn(cs_c[i], make_float2(va[2 * i], va[2 * i + 1]), acc[0]);
-          acc[1] = __ffma2_rn(cs_c[i + 1], make_float2(va[2 * i + 2], va[2 * i + 3]), acc[1]);
-          acc[2] = __ffma2_rn(cs_s[i], make_float2(vc[2 * i], vc[2 * i + 1]), acc[2]);
-          acc[3] = __ffma2_rn(cs_s[i + 1], make_float2(vc[2 * i + 2], vc[2 * i + 3]), acc[3]);
+        for (int q = 0; q < 8; ++q) {                    // columns [16q, 16q + 16): q < 4 cosine part, else sine part
+          float v[16];
+          tmem_ld16(ta + 16u * q, v);
+          if (q == 7) {                                  // accumulator free for the MMA of job j + kKAcc
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(d_empty + db);
+          }
+          const int f0 = (q & 3) * 8;                    // first frequency pair of this block
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) {
+            if (q < 4) {
+              acc0 = __ffma2_rn(cs_c[f0 + i], make_float2(v[2 * i], v[2 * i + 1]), acc0);
+              acc1 = __ffma2_rn(cs_c[f0 + i + 1], make_float2(v[2 * i + 2], v[2 * i + 3]), acc1);
+            } else {
+              acc0 = __ffma2_rn(cs_s[f0 + i], make_float2(v[2 * i], v[2 * i + 1]), acc0);
+              acc1 = __ffma2_rn(cs_s[f0 + i + 1], make_float2(v[2 * i + 2], v[2 * i + 3]), acc1);
+            }
+          }
         }
-        const float part = ((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y)) + ((acc[2].x + acc[2].y) + (acc[3].x + acc[3].y));
-        const int pk = j % kKPartRing;
-        if (!mbar_wait(part_empty + pk, (uint32_t)(((j / kKPartRing) & 1) ^ 1))) { ok = false; break; }
-        s_part[pk * 256 + 128 * h + row] = part;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(part_full + pk);
+        if (row == 0) stamp(j, kTrDrainLd);
+        const float sum = (acc0.x + acc0.y) + (acc1.x + acc1.y);
+        const int l = t_begin + tile * 128 + row;
+        if (l < t_end) {
+          float val = sum * s_epi[g];
+          if (p.mask) val = fmaf(p.mask[(int64_t)b * p.T + l], p.mask_scale, val);
+          lg_base[(int64_t)g * p.T + tile * 128] = val;
+#pragma unroll
+          for (int gg = 0; gg < G; ++gg)
+            if (gg == g) m_run[gg] = fmaxf(m_run[gg], val);
+        }
+        if (row == 0) stamp(j, kTrDrainDone);
+        db += 2;
+        if (db >= kKAcc) { db -= kKAcc; dph ^= 1u; }
       }
       if (!ok) fail(kDevWaitMma);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float m = m_run[g];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_red[g * 8 + w2 * 4 + dw] = m;
+      }
     }
   }
 
@@ -672,7 +688,9 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   const unsigned long long w_done = w_done_s;
 #endif
   if (p.smax && tid < G && !*s_abort) {
-    const float M = fmaxf(s_red[tid * 8], s_red[tid * 8 + 1]);
+    float M = s_red[tid * 8];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) M = fmaxf(M, s_red[tid * 8 + k]);
     p.smax[((int64_t)b * Hq + grp * G + tid) * p.nsplit + split] = M;
   }
   if (warp == 0) {

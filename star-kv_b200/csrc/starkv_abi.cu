@@ -83,7 +83,7 @@ int k_elem_bytes(const starkv_layout& l) { return l.quantized ? 1 : dtype_bytes(
 // K-path geometry: heads per CTA (G) and the shared memory that fits (one CTA
 // per SM: it owns all 512 TMEM columns).
 struct KGeom {
-  int G, rmax, bsum, pitch16max, nstages;
+  int G, rmax, bsum, stage_total;
   size_t smem;
 };
 
@@ -92,27 +92,27 @@ KGeom k_geometry(const starkv_layout& l) {
   g.rmax = max_k_rank(l);
   const int xb = k_elem_bytes(l);
   const int Hq = l.num_q_heads, qpk = l.num_q_heads / l.num_kv_heads;
-  g.pitch16max = 0;
-  for (int h = 0; h < l.num_kv_heads; ++h) {
-    const int pt = k_pitch16(l.k_rank[h], xb);
-    g.pitch16max = pt > g.pitch16max ? pt : g.pitch16max;
-  }
-  // Largest G whose W matrices leave room for a staging ring of >= 3 stages (2 at G = 1).
+  // Largest G whose W matrices leave room for a staging ring of >= 2 tile slots
+  // (a tile slot: 128 rows of every distinct KV head of the group).
   for (int G = 4; G >= 1; G >>= 1) {
     if (Hq % G) continue;
-    int bsum = 0;
+    int bsum = 0, tmax = 0;
     for (int grp = 0; grp < Hq / G; ++grp) {
-      int s = 0;
-      for (int k = 0; k < G; ++k) s += l.k_rank[(grp * G + k) / qpk];
+      int s = 0, tb = 0;
+      for (int k = 0; k < G; ++k) {
+        const int kv = (grp * G + k) / qpk;
+        s += l.k_rank[kv];
+        if (k == 0 || kv != (grp * G + k - 1) / qpk) tb += 128 * l.k_rank[kv] * xb;
+      }
       bsum = s > bsum ? s : bsum;
+      tmax = tb > tmax ? tb : tmax;
     }
-    const int ns = k_stages_fit(bsum, g.pitch16max);
-    if (ns >= (G == 1 ? 2 : 3)) {
+    const long st = k_stage_total(bsum);
+    if (st >= 2L * tmax) {
       g.G = G;
       g.bsum = bsum;
-      g.nstages = ns;
-      const size_t bytes = k_smem_bytes(bsum, g.pitch16max, ns);
-      g.smem = bytes < 116 * 1024 ? 116 * 1024 : bytes;  // never two CTAs (2 x 512 TMEM columns) per SM
+      g.stage_total = (int)st;
+      g.smem = (size_t)kKSmemMax;                // one CTA per SM (it owns all 512 TMEM columns)
       return g;
     }
   }
@@ -120,7 +120,7 @@ KGeom k_geometry(const starkv_layout& l) {
   g.bsum = 0;
   g.smem = 0;
   g.rmax = 0;
-  g.nstages = 0;
+  g.stage_total = 0;
   return g;
 }
 
@@ -356,8 +356,7 @@ int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp
   kp.G = g.G;
   kp.rmax = g.rmax;
   kp.bsum = g.bsum;
-  kp.pitch16max = g.pitch16max;
-  kp.nstages = g.nstages;
+  kp.stage_total = g.stage_total;
   kp.inv_freq = a->inv_freq;
   kp.trace = g_trace;
   kp.trace_jobs = g_trace_jobs;
