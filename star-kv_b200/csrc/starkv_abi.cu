@@ -158,15 +158,14 @@ V2Geom v2_geometry(const starkv_layout& l) {
   if (!l.quantized) return g;
   const int Hq = l.num_q_heads, qpk = Hq / l.num_kv_heads, R = l.v_rank_total;
   if (Hq > kV2MaxHeads || Hq % 8) return g;
-  int gmax = 0, units = 0;
-  for (int j = 0; j < l.num_v_blocks; ++j) {
-    gmax = l.v_num_kv[j] * qpk > gmax ? l.v_num_kv[j] * qpk : gmax;
-    units += (l.v_rank[j] + 127) / 128;
-  }
-  g.np = gmax <= 16 ? 16 : 32;
-  if (gmax > 32 || units > kV2MaxUnits || units * g.np > 512) return g;
+  (void)qpk;
+  // M units are consecutive 128-channel ranges of the whole latent row; every
+  // unit's MMA covers all query heads (N = np >= Hq), one shared B tile.
+  const int units = (R + 127) / 128;
+  g.np = Hq <= 16 ? 16 : 32;
+  if (Hq > 32 || units > kV2MaxUnits || units * g.np > 512) return g;
   g.stage_bytes = v2_stage_bytes(R);
-  g.b_bytes = l.num_v_blocks * g.np * 128;
+  g.b_bytes = g.np * 128;
   const long fixed = (long)kV2Header + (long)kV2Abufs * kV2ABytes + 2L * g.b_bytes;
   long ns = (227L * 1024 - fixed) / g.stage_bytes;
   if (ns > kV2MaxStages) ns = kV2MaxStages;

@@ -346,27 +346,28 @@ __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ Co
 
 // ============================================================================
 // Decode V path, streaming form (int4 latents): CTA = (V split, sequence b), all
-// V blocks and all query heads of the layer, one CTA per SM.
+// V blocks and all query heads of the layer, one CTA per SM, 512 threads.
 //
 // A 64-token tile of one sequence is one contiguous block of int4 codes
 // (64 x R/2 bytes) and one of fp16 (scale, zero) pairs (64 x R/8 bytes) in HBM:
-//   producer warp:  1-D bulk copies of both into a ring of shared-memory stages;
-//   dequant warps (8, four pairs): per (V block, 128-channel M tile) "M unit",
-//                   q*s + z (one fp16 rounding) into one of 4 MN-major A tiles (128
-//                   channels x 64 tokens); pair p owns A tile p, so four M units
-//                   are converted at once;
+//   producer warp:  1-D bulk copies of both into a ring of shared-memory stages,
+//                   and an L2 prefetch of the tile's logits;
+//   dequant warps (12, six pairs): per "M unit" = 128 consecutive channels of the
+//                   whole latent row, q*s + z (one fp16 rounding, channels in the
+//                   order [0,4,1,5,2,6,3,7] within every 8) into one of 6 MN-major
+//                   A tiles (128 channels x 64 tokens); pair p owns A tile p;
 //   prob warps (2): p = exp2(logit - M_h) for every head (M_h = maximum over the
-//                   K splits), fp16(p * 2^12) into per-block K-major B tiles
+//                   K splits), fp16(p * 2^12) into one K-major B tile of all heads
 //                   (double-buffered by tile), and the running sum of p;
-//   MMA thread:     4 tcgen05.mma (M=128, N=NP, K=16) per M unit and tile into
-//                   the M unit's accumulator D[channel, head] in TMEM.
+//   MMA thread:     4 tcgen05.mma (M=128, N=NP >= Hq, K=16) per M unit and tile
+//                   into the unit's accumulator D[channel, head] in TMEM.
 // At the end the dequant warps read the accumulators and write the split
-// partials; the prob warps write the split sums of p.  The combine kernel
-// divides by the total sum.
+// partials of each channel's own V block heads; the prob warps write the split
+// sums of p.  The combine kernel divides by the total sum.
 // ============================================================================
-constexpr int kV2Threads = 384;
+constexpr int kV2Threads = 512;
 constexpr int kV2Tile = 64;
-constexpr int kV2Abufs = 4;
+constexpr int kV2Abufs = 6;        // one per dequant warp pair
 constexpr int kV2ABytes = 16384;     // 128 channels x 64 tokens fp16
 constexpr int kV2Header = 2048;
 constexpr int kV2MaxStages = 4;
@@ -391,10 +392,71 @@ struct V2Params {
 enum V2Trace { kV2TrIssue = 0, kV2TrStage, kV2TrDequant, kV2TrProbs, kV2TrMmaB, kV2TrMmaDone, kV2TrFields = 8 };
 
 __host__ __device__ inline int v2_stage_bytes(int R) {
-  return ((kV2Tile * (R / 2) + kV2Tile * (R / 8) + 16) + 127) & ~127;
+  return ((kV2Tile * (R / 2) + kV2Tile * (R / 8) + 32) + 127) & ~127;
+}
+
+// End (exclusive) of the staged parameter bytes of a tile whose rows end at byte
+// `end`: rounded up to 16 bytes unless that would pass the buffer's end.
+__host__ __device__ inline int64_t v2_param_end(int64_t end, int64_t total) {
+  const int64_t up = (end + 15) & ~(int64_t)15;
+  return up <= total ? up : (end & ~(int64_t)15);
 }
 __host__ __device__ inline size_t v2_smem_bytes(int nstages, int stage_bytes, int b_bytes) {
   return (size_t)kV2Header + (size_t)nstages * stage_bytes + (size_t)kV2Abufs * kV2ABytes + 2 * (size_t)b_bytes;
+}
+
+// 32 int4 codes (16 bytes, even channel in the low nibble) -> 4 x 8 fp16 of q*s + z
+// in the channel order [0, 4, 1, 5, 2, 6, 3, 7] within every 8 (one LOP3 puts two
+// nibbles under the 0x6400 exponent; the subtraction of 1024 (or of 1024 for a
+// nibble scaled by 16) is exact, the fused q*s + z one rounding; s16 = s / 16).
+__device__ __forceinline__ void dequant32_i4_perm(const uint4 w, __half2 s2, __half2 s16, __half2 z2, uint4* out) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  const __half2 k1024 = __half2half2(__ushort_as_half((unsigned short)0x6400));
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const uint32_t w8 = ws[u] >> 8;
+    uint32_t a = (ws[u] & 0x000F000Fu) | 0x64006400u;   // channels 0, 4
+    uint32_t c = (ws[u] & 0x00F000F0u) | 0x64006400u;   // channels 1, 5 (x16)
+    uint32_t e = (w8 & 0x000F000Fu) | 0x64006400u;      // channels 2, 6
+    uint32_t g = (w8 & 0x00F000F0u) | 0x64006400u;      // channels 3, 7 (x16)
+    __half2 ha = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&a), k1024), s2, z2);
+    __half2 hc = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&c), k1024), s16, z2);
+    __half2 he = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&e), k1024), s2, z2);
+    __half2 hg = __hfma2(__hsub2(*reinterpret_cast<__half2*>(&g), k1024), s16, z2);
+    out[u] = make_uint4(*reinterpret_cast<uint32_t*>(&ha), *reinterpret_cast<uint32_t*>(&hc),
+                        *reinterpret_cast<uint32_t*>(&he), *reinterpret_cast<uint32_t*>(&hg));
+  }
+}
+
+// Channel held at position j (0..7) of a dequant32_i4_perm 8-channel row.
+__host__ __device__ constexpr int v_perm8(int j) { return (j >> 1) + 4 * (j & 1); }
+
+// Dequantise one M unit (GC groups of 32 channels x 64 tokens) into an MN-major A tile.
+// Item it = (token, group); 8 consecutive lanes = 8 tokens of one group, so every
+// 16-byte store phase covers 128 contiguous bytes.  pl = lane within the warp pair.
+template <int GC>
+__device__ __forceinline__ void v2_dequant_unit(const uint8_t* codes, const uint8_t* pars, const uint8_t* gpars,
+                                                int pdelta, int pcopied, int c0, int nrows, int code_row,
+                                                int par_row, uint8_t* A, int pl) {
+#pragma unroll
+  for (int k = 0; k < GC; ++k) {
+    const int row8 = (pl >> 3) + 8 * k;
+    const int grp = row8 % GC, l = (row8 / GC) * 8 + (pl & 7);
+    uint4 o[4] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u),
+                  make_uint4(0u, 0u, 0u, 0u)};
+    if (l < nrows) {
+      const uint4 w = *reinterpret_cast<const uint4*>(codes + l * code_row + (c0 >> 1) + grp * 16);
+      const int po = l * par_row + ((c0 >> 5) + grp) * 4;
+      const uint32_t pz = pdelta + po + 4 <= pcopied ? *reinterpret_cast<const uint32_t*>(pars + pdelta + po)
+                                                     : *reinterpret_cast<const uint32_t*>(gpars + po);
+      const __half2 sz = *reinterpret_cast<const __half2*>(&pz);
+      const __half2 s2 = __half2half2(__low2half(sz));
+      dequant32_i4_perm(w, s2, __hmul2(s2, __half2half2(__float2half_rn(0.0625f))), __half2half2(__high2half(sz)), o);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      *reinterpret_cast<uint4*>(A + (grp * 4 + u) * 1024 + (l >> 3) * 128 + (l & 7) * 16) = o[u];
+  }
 }
 
 // 8 int4 codes (4 bytes, even channel in the low nibble) -> 8 fp16 of q*s + z.
@@ -425,21 +487,20 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
   const int ntiles = t_end > t_begin ? (t_end - t_begin + kV2Tile - 1) / kV2Tile : 0;
   const int NS = p.nstages;
   const int code_row = R / 2, par_row = R / 8;
+  const int64_t ptotal = (int64_t)lay.batch * lay.capacity * par_row;   // bytes of the parameter buffer
 
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 1536);
   uint64_t* st_full = bars;            // [4]
-  uint64_t* st_empty = bars + 4;       // [4]  8 dequant warps
-  uint64_t* a_full = bars + 8;         // [4]  the slot's dequant warp pair
-  uint64_t* a_empty = bars + 12;       // [4]  commit
-  uint64_t* b_full = bars + 16;        // [2]  2 prob warps
-  uint64_t* b_empty = bars + 18;       // [2]  commit
-  uint64_t* fin_bar = bars + 20;
+  uint64_t* st_empty = bars + 4;       // [4]  12 dequant warps
+  uint64_t* a_full = bars + 8;         // [6]  the slot's dequant warp pair
+  uint64_t* a_empty = bars + 14;       // [6]  commit
+  uint64_t* b_full = bars + 20;        // [2]  2 prob warps
+  uint64_t* b_empty = bars + 22;       // [2]  commit
+  uint64_t* fin_bar = bars + 24;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 192);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 196);
   int* s_nunits = reinterpret_cast<int*>(smem + 200);
-  uint8_t* s_ublk = smem + 256;                               // [64] V block of M unit m
-  uint8_t* s_umt = smem + 320;                                // [64] M tile of M unit m
-  int* s_boffB = reinterpret_cast<int*>(smem + 384);          // [32] B tile offset of V block
+  uint8_t* s_cblk = smem + 256;                               // [kV2MaxUnits * 4] V block of each 32-channel group
   float* s_mx = reinterpret_cast<float*>(smem + 512);         // [64] softmax maximum per head
   float* s_ps = reinterpret_cast<float*>(smem + 768);         // [2][64] prob-warp sums
   uint8_t* Ssm = smem + kV2Header;
@@ -449,7 +510,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
   if (tid == 0) {
     for (int k = 0; k < kV2MaxStages; ++k) {
       mbar_init(st_full + k, 1);
-      mbar_init(st_empty + k, 8);
+      mbar_init(st_empty + k, 12);
     }
     for (int k = 0; k < kV2Abufs; ++k) {
       mbar_init(a_full + k, 2);        // the slot's warp pair
@@ -461,15 +522,9 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
     }
     mbar_init(fin_bar, 1);
     *s_abort = 0;
-    int m = 0;
-    for (int j = 0; j < lay.num_v_blocks; ++j) {
-      s_boffB[j] = j * NP * 128;
-      for (int mt = 0; mt * 128 < lay.v_rank[j]; ++mt, ++m) {
-        s_ublk[m] = (uint8_t)j;
-        s_umt[m] = (uint8_t)mt;
-      }
-    }
-    *s_nunits = m;
+    for (int j = 0; j < lay.num_v_blocks; ++j)
+      for (int c = lay.v_col[j]; c < lay.v_col[j] + lay.v_rank[j]; c += 32) s_cblk[c >> 5] = (uint8_t)j;
+    *s_nunits = (R + 127) / 128;
     fence_mbar_init();
   }
   // zero the B tiles once: padded heads stay zero
@@ -507,15 +562,24 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         const int nrows = min(kV2Tile, t_end - t0);
         const int64_t row0 = (int64_t)b * lay.capacity + t0;
         const uint32_t cb = (uint32_t)(nrows * code_row);
-        // parameters: the 16-byte-aligned span inside [row0, row0 + nrows) rows;
-        // the unaligned tail is read from global by the dequant warps
+        // parameters: [row0, row0 + nrows) rows widened to 16-byte boundaries, the end
+        // rounded down only at the end of the buffer (that tail is read from global
+        // by the dequant warps)
         const int64_t pstart = row0 * par_row, pa = pstart & ~(int64_t)15;
-        const int64_t pend = (pstart + (int64_t)nrows * par_row) & ~(int64_t)15;
+        const int64_t pend = v2_param_end(pstart + (int64_t)nrows * par_row, ptotal);
         const uint32_t pb = pend > pa ? (uint32_t)(pend - pa) : 0u;
         mbar_arrive_expect_tx(st_full + s, cb + pb);
         uint8_t* dst = Ssm + (size_t)s * p.stage_bytes;
         bulk_g2s(dst, p.v_cache + row0 * code_row, cb, st_full + s);
         if (pb) bulk_g2s(dst + kV2Tile * code_row, p.v_params + pa, pb, st_full + s);
+        // the tile's logits (one row of nrows floats per head) into L2 for the prob
+        // warps: the 16-byte-aligned span inside each row (a hint; the ends are
+        // loaded from HBM)
+        for (int h = 0; h < Hq; ++h) {
+          const uintptr_t a0 = reinterpret_cast<uintptr_t>(p.logits + ((int64_t)b * Hq + h) * p.T + t0);
+          const uintptr_t lo = (a0 + 15) & ~(uintptr_t)15, hi = (a0 + (uintptr_t)nrows * 4) & ~(uintptr_t)15;
+          if (hi > lo) bulk_prefetch_l2(reinterpret_cast<const void*>(lo), (uint32_t)(hi - lo));
+        }
       }
       for (int t = max(0, issued - NS); t < issued; ++t)
         if (!mbar_wait(st_full + (t % NS), (uint32_t)((t / NS) & 1))) { fail(kDevWaitCopy); break; }
@@ -534,12 +598,12 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         stamp(t, kV2TrMmaB);
         const uint32_t bt = smem_u32(Bsm + tb * p.b_bytes);
         for (int m = 0; m < MU; ++m, ++mc) {
-          const int k = mc & (kV2Abufs - 1);
+          const int k = mc % kV2Abufs;
           if (!mbar_wait(a_full + k, (uint32_t)((mc / kV2Abufs) & 1))) { ok = false; break; }
           tc_fence_after();
           if (mtrace && mc < p.trace_tiles) mtrace[mc * 4 + 2] = clock64();
           const uint64_t ad = smem_desc(smem_u32(Asm + k * kV2ABytes), 128, 1024);
-          const uint64_t bd = smem_desc(bt + (uint32_t)s_boffB[s_ublk[m]], 128, 1024);
+          const uint64_t bd = smem_desc(bt, 128, 1024);
           const uint32_t d = tmem + (uint32_t)(m * NP);
 #pragma unroll
           for (int ks = 0; ks < kV2Tile / 16; ++ks)
@@ -574,28 +638,29 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       mh[q] = 0.f;
       psum[q] = 0.f;
       if (q < G8) {
-        const int g = q * 8 + (lane & 7), kv = g / qpk;
-        int blk = 0;
-        while (blk + 1 < lay.num_v_blocks && lay.v_first_kv[blk + 1] <= kv) ++blk;
-        const int gl = g - lay.v_first_kv[blk] * qpk;
-        dstoff[q] = s_boffB[blk] + (gl >> 3) * 1024 + (gl & 7) * 16;
+        const int g = q * 8 + (lane & 7);
+        dstoff[q] = (g >> 3) * 1024 + (g & 7) * 16;
         mh[q] = s_mx[g];
       }
     }
     const int kb = (lane >> 3) + 4 * pw;           // 8-token block of the tile
-    bool ok = true;
-    for (int t = 0; t < ntiles; ++t) {
-      if (*s_abort) break;
-      const int tb = t & 1;
+    auto load_lg = [&](int t, float (&lg)[kV2MaxHeads / 8][8]) {
       const int l0 = t_begin + t * kV2Tile + kb * 8;
-      float lg[kV2MaxHeads / 8][8];
 #pragma unroll
       for (int q = 0; q < kV2MaxHeads / 8; ++q)
         if (q < G8) {
           const float* src = p.logits + ((int64_t)b * Hq + q * 8 + (lane & 7)) * p.T + l0;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) lg[q][e] = (l0 + e < t_end) ? src[e] : kNegBig;
+          for (int e = 0; e < 8; ++e) lg[q][e] = (t < ntiles && l0 + e < t_end) ? __ldg(src + e) : kNegBig;
         }
+    };
+    float lg[kV2MaxHeads / 8][8];
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) {
+      if (*s_abort) break;
+      const int tb = t & 1;
+      const int l0 = t_begin + t * kV2Tile + kb * 8;
+      load_lg(t, lg);
       if (!mbar_wait(b_empty + tb, (uint32_t)(((t >> 1) & 1) ^ 1))) { ok = false; break; }
       uint8_t* Bt = Bsm + tb * p.b_bytes + kb * 128;
 #pragma unroll
@@ -629,9 +694,9 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       for (int h = pt; h < Hq; h += 64) p.lsum[((int64_t)b * Hq + h) * p.nsplit + split] = s_ps[h] + s_ps[64 + h];
   } else {
     // ============================================================ dequant warps
-    // Four warp pairs: pair p fills A slot p with the M units whose running
-    // index mc = t * MU + m is p mod 4, so four M units are in flight.
-    const int dw = warp - 4;                       // 0..7
+    // Six warp pairs: pair p fills A slot p with the M units whose running
+    // index mc = t * MU + m is p mod 6, so six M units are in flight.
+    const int dw = warp - 4;                       // 0..11
     const int pair = dw >> 1, pl = (dw & 1) * 32 + lane;
     int mc = 0;
     bool ok = true;
@@ -646,42 +711,23 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       const int nrows = min(kV2Tile, t_end - t0);
       const int64_t pstart = ((int64_t)b * lay.capacity + t0) * par_row;
       const int pdelta = (int)(pstart & 15);                // stage byte of parameter row 0
-      const int64_t pend = (pstart + (int64_t)nrows * par_row) & ~(int64_t)15;
+      const int64_t pend = v2_param_end(pstart + (int64_t)nrows * par_row, ptotal);
       const int pcopied = pend > (pstart & ~(int64_t)15) ? (int)(pend - (pstart & ~(int64_t)15)) : 0;
       const uint8_t* gpars = p.v_params + pstart;
       for (int m = 0; m < MU; ++m, ++mc) {
-        const int k = mc & (kV2Abufs - 1);
+        const int k = mc % kV2Abufs;
         if (k != pair) continue;
         if (!mbar_wait(a_empty + k, (uint32_t)(((mc / kV2Abufs) & 1) ^ 1))) { ok = false; break; }
         if (mtrace && mc < p.trace_tiles && pl == 0) mtrace[mc * 4 + 0] = clock64();
-        const int blk = s_ublk[m], mt = s_umt[m];
-        const int c0 = lay.v_col[blk] + mt * 128;            // first global channel of the M tile
-        const int nch = min(128, lay.v_rank[blk] - mt * 128);
+        const int c0 = m * 128;                              // first global channel of the M unit
+        const int nch = min(128, R - c0);
         const int gc = nch >> 5;                             // 32-channel groups in the M tile
         uint8_t* A = Asm + k * kV2ABytes;
-        // item = (token, 32-channel group); 8 consecutive lanes = 8 tokens of one
-        // group, so every 16-byte store phase covers 128 contiguous bytes
-#pragma unroll 2
-        for (int it = pl; it < gc * kV2Tile; it += 64) {
-          const int grp = (it >> 3) % gc, l = ((it >> 3) / gc) * 8 + (it & 7);
-          uint4 o[4] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u),
-                        make_uint4(0u, 0u, 0u, 0u)};
-          if (l < nrows) {
-            const uint4 w = *reinterpret_cast<const uint4*>(codes + l * code_row + (c0 >> 1) + grp * 16);
-            const int po = l * par_row + ((c0 >> 5) + grp) * 4;
-            const uint32_t pz = pdelta + po + 4 <= pcopied ? *reinterpret_cast<const uint32_t*>(pars + pdelta + po)
-                                                           : *reinterpret_cast<const uint32_t*>(gpars + po);
-            const __half2 sz = *reinterpret_cast<const __half2*>(&pz);
-#ifdef V2_NODQ
-            o[0] = w; o[1] = w; o[2] = w; o[3] = make_uint4(pz, 0u, 0u, 0u);
-            (void)sz;
-#else
-            dequant32_i4(w, __half2half2(__low2half(sz)), __half2half2(__high2half(sz)), o);
-#endif
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            *reinterpret_cast<uint4*>(A + (grp * 4 + u) * 1024 + (l >> 3) * 128 + (l & 7) * 16) = o[u];
+        switch (gc) {
+          case 1: v2_dequant_unit<1>(codes, pars, gpars, pdelta, pcopied, c0, nrows, code_row, par_row, A, pl); break;
+          case 2: v2_dequant_unit<2>(codes, pars, gpars, pdelta, pcopied, c0, nrows, code_row, par_row, A, pl); break;
+          case 3: v2_dequant_unit<3>(codes, pars, gpars, pdelta, pcopied, c0, nrows, code_row, par_row, A, pl); break;
+          default: v2_dequant_unit<4>(codes, pars, gpars, pdelta, pcopied, c0, nrows, code_row, par_row, A, pl); break;
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -698,8 +744,9 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
     if (have && !mbar_wait(fin_bar, 0)) fail(kDevWaitMma);
     tc_fence_after();
     const int q4 = warp & 3;
-    for (int m = dw >> 2; m < MU; m += 2) {
-      const int blk = s_ublk[m], mt = s_umt[m];
+    for (int m = dw >> 2; m < MU; m += 3) {
+      const int cg = m * 128 + q4 * 32 + (lane & ~7) + v_perm8(lane & 7);   // global channel of this lane's row
+      const int blk = cg < R ? s_cblk[cg >> 5] : 0;
       const int Gv = lay.v_num_kv[blk] * qpk, qh0 = lay.v_first_kv[blk] * qpk;
       float d[NP];
       const uint32_t ta = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(m * NP);
@@ -710,12 +757,12 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
 #pragma unroll
         for (int g = 0; g < NP; ++g) d[g] = 0.f;
       }
-      const int c = mt * 128 + q4 * 32 + lane;               // channel within the V block
-      if (c < lay.v_rank[blk]) {
+      const int c = cg - lay.v_col[blk];                     // channel within the V block
+      if (cg < R) {
 #pragma unroll
         for (int g = 0; g < NP; ++g)
-          if (g < Gv)
-            p.partial[(((int64_t)b * Hq + qh0 + g) * p.nsplit + split) * p.rv_max + c] = d[g] * (1.f / kVPScale);
+          if (g >= qh0 && g < qh0 + Gv)
+            p.partial[(((int64_t)b * Hq + g) * p.nsplit + split) * p.rv_max + c] = d[g] * (1.f / kVPScale);
       }
     }
   }
