@@ -343,10 +343,10 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   uint64_t* st_empty = bars + 32;                // [32] unit slot read by the 4 converter warps
   uint64_t* a_full = bars + 64;                  // [2]  A buffer written (4 converter warps)
   uint64_t* a_empty = bars + 80;                 // [2]  A buffer's MMAs retired (commit)
-  uint64_t* d_full = bars + 96;                  // [3]  accumulator ready (commit)
-  uint64_t* d_empty = bars + 99;                 // [3]  accumulator read by the job's 4 drain warps
-  uint64_t* fin_bar = bars + 102;
-  uint64_t* w_bar = bars + 103;                  // W images landed (pre-pass mode)
+  uint64_t* d_full = bars + 96;                  // [6]  job slot j % 6: accumulator j % 3 ready (commit)
+  uint64_t* d_empty = bars + 102;                // [6]  job slot j % 6: accumulator read by the job's 4 drain warps
+  uint64_t* fin_bar = bars + 108;
+  uint64_t* w_bar = bars + 109;                  // W images landed (pre-pass mode)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 512);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 516);
   int* s_nruns = reinterpret_cast<int*>(smem + 520);
@@ -374,11 +374,10 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       mbar_init(a_full + k, 4);
       mbar_init(a_empty + k, 1);
     }
-    for (int k = 0; k < kKAcc; ++k) {
+    for (int k = 0; k < 2 * kKAcc; ++k) {
       mbar_init(d_full + k, 1);
       mbar_init(d_empty + k, 4);       // the drain warpgroup of the job
     }
-    mbar_init(fin_bar, 1);
     mbar_init(w_bar, 1);
     *s_abort = 0;
     int off = 0, nr = 0;
@@ -396,6 +395,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       ++s_runlen[nr - 1];
     }
     *s_nruns = nr;
+    mbar_init(fin_bar, nr == G ? 2 : 1);       // one arrival per MMA issuer
     int tb = 0;
     for (int n = 0; n < nr; ++n) {
       s_runoff[n] = tb;
@@ -465,49 +465,47 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         }
       }
       __syncwarp();
-    } else if (warp == 1) {
-      // ============================================================ MMA issuer
+    } else if (warp == 1 || warp == 2) {
+      // ============================================================ MMA issuers
+      // When every query head of the group has its own KV head (one job per unit),
+      // warps 1 and 2 issue the units of parity 0 and 1 (the bookkeeping of one
+      // overlaps the MMAs of the other); otherwise warp 1 issues every unit.  Job j
+      // accumulates into accumulator j % 3 and signals job slot j % 6 (one job
+      // parity per slot, so each slot's phases are waited in order by one issuer and
+      // one drain warpgroup); before reusing accumulator j % 3 the issuer waits for
+      // job j - 3 to be drained (slot (j - 3) % 6, at most one phase behind: this
+      // issuer waited for job j - 9 before it issued job j - 6).
       named_bar_sync(1, 512 + 96);               // W matrices built (builders + warps 1-3)
-      if (p.wpre && lane == 0 && !mbar_wait(w_bar, 0)) fail(kDevWaitCopy);
-      if (lane == 0) {
+      const int NI = (NR == G) ? 2 : 1;          // issuers
+      const int iw = warp - 1;
+      if (iw < NI && lane == 0) {
+        if (p.wpre && !mbar_wait(w_bar, 0)) fail(kDevWaitCopy);
         constexpr uint32_t IDESC = idesc_f16_f32(128, 128);
-        // Per-head operands in registers (G is a compile-time constant, so every
-        // index below is static): B descriptor, K steps, and whether the head
-        // starts a run of heads that share one A buffer (one KV head).
-        uint64_t bdesc[G];
-        int nk[G];
-        bool first[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          bdesc[g] = smem_desc(smem_u32(Bsm + s_boff[g]), 128, (uint32_t)s_rank[g] * 16u);
-          nk[g] = s_rank[g] >> 4;
-          first[g] = g == 0 || (grp * G + g) / qpk != (grp * G + g - 1) / qpk;
-        }
         bool ok = true;
-        int u = -1;                                // current unit
-        uint32_t a_t = 0;
-        int db = 0;                                // accumulator of job j = j % kKAcc, and its phase
-        uint32_t dph = 0;
-        for (int t = 0; t < ntiles && ok; ++t) {
-          if (*s_abort) break;
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const int j = t * G + g;
-            if (first[g]) {
-              ++u;
-              if (!mbar_wait(a_full + (u & 1), (uint32_t)((u >> 1) & 1))) { ok = false; break; }
-              a_t = tmem + 384u + (uint32_t)(u & 1) * 64u;
+        int t = 0, n = iw;                         // tile and run of unit u
+        if (n >= NR) { n -= NR; ++t; }
+        for (int u = iw; u < U && ok; u += NI) {
+          if (!mbar_wait(a_full + (u & 1), (uint32_t)((u >> 1) & 1))) { ok = false; break; }
+          const uint32_t a_t = tmem + 384u + (uint32_t)(u & 1) * 64u;
+          const int g0 = s_run0[n], len = s_runlen[n];
+          for (int k = 0; k < len; ++k) {
+            const int g = g0 + k, j = t * G + g;
+            if (j >= kKAcc) {
+              const int jp = j - kKAcc;
+              if (!mbar_wait(d_empty + jp % (2 * kKAcc), (uint32_t)((jp / (2 * kKAcc)) & 1))) { ok = false; break; }
             }
-            if (!mbar_wait(d_empty + db, dph ^ 1u)) { ok = false; break; }
             tc_fence_after();
             stamp(j, kTrMmaIssue);
-            const uint32_t d = tmem + (uint32_t)db * 128u;
-            mma_f16_ts(d, a_t, bdesc[g], IDESC, 0u);
-            for (int kk = 1; kk < nk[g]; ++kk) mma_f16_ts(d, a_t + kk * 8, bdesc[g] + (uint64_t)(kk * 16), IDESC, 1u);
-            mma_commit(d_full + db);
-            if (g == G - 1 || first[(g + 1) % G]) mma_commit(a_empty + (u & 1));
-            if (++db == kKAcc) { db = 0; dph ^= 1u; }
+            const int r = s_rank[g];
+            const uint64_t bdesc = smem_desc(smem_u32(Bsm + s_boff[g]), 128, (uint32_t)r * 16u);
+            const uint32_t d = tmem + (uint32_t)(j % kKAcc) * 128u;
+            mma_f16_ts(d, a_t, bdesc, IDESC, 0u);
+            for (int kk = 1; kk < (r >> 4); ++kk) mma_f16_ts(d, a_t + kk * 8, bdesc + (uint64_t)(kk * 16), IDESC, 1u);
+            mma_commit(d_full + j % (2 * kKAcc));
           }
+          mma_commit(a_empty + (u & 1));
+          n += NI;
+          while (n >= NR) { n -= NR; ++t; }
         }
         if (!ok) fail(kDevWaitMma);
         mma_commit(fin_bar);                     // arrives once every MMA of this thread retired
@@ -515,7 +513,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       }
       __syncwarp();
     } else {
-      // warps 2, 3: no role after the prologue barrier
+      // warp 3: no role after the prologue barrier
       named_bar_sync(1, 512 + 96);
     }
   } else {
@@ -610,9 +608,10 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       const uint32_t lbase = tmem + ((uint32_t)(dw * 32) << 16);
       float* const lg_base = p.logits + ((int64_t)b * Hq + grp * G) * p.T + t_begin + row;
       bool ok = true;
-      int db = w2;                                       // accumulator of job j = j % kKAcc and its phase
+      int ds = w2;                                       // job slot j % 6 and its phase
       uint32_t dph = 0;
       for (int j = w2; j < J && ok; j += 2) {
+        const int db = j % kKAcc;                        // accumulator
         if (*s_abort) { ok = false; break; }
         const int tile = j / G, g = j - tile * G;
         for (; cur_tile < tile; ++cur_tile) {            // advance every frequency by 128 positions
@@ -628,7 +627,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
           }
         }
         if (row == 0) stamp(j, kTrDrainWait);
-        if (!mbar_wait(d_full + db, dph)) { ok = false; break; }
+        if (!mbar_wait(d_full + ds, dph)) { ok = false; break; }
         tc_fence_after();
         if (row == 0) stamp(j, kTrDrainGot);
         const uint32_t ta = lbase + (uint32_t)db * 128u;
@@ -640,7 +639,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
           if (q == 7) {                                  // accumulator free for the MMA of job j + kKAcc
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty + db);
+            if (lane == 0) mbar_arrive(d_empty + ds);
           }
           const int f0 = (q & 3) * 8;                    // first frequency pair of this block
 #pragma unroll
@@ -666,8 +665,8 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
             if (gg == g) m_run[gg] = fmaxf(m_run[gg], val);
         }
         if (row == 0) stamp(j, kTrDrainDone);
-        db += 2;
-        if (db >= kKAcc) { db -= kKAcc; dph ^= 1u; }
+        ds += 2;
+        if (ds >= 2 * kKAcc) { ds -= 2 * kKAcc; dph ^= 1u; }
       }
       if (!ok) fail(kDevWaitMma);
 #pragma unroll
