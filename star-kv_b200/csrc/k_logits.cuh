@@ -86,8 +86,8 @@ enum KTrace {
 
 constexpr int kKThreads = 640;
 // Register budget per warpgroup after setmaxnreg: control, two converters, two
-// drains (40 + 2*56 + 2*160 = 472 <= 5 * 96, the launch budget).
-constexpr int kKCtlRegs = 40, kKConvRegs = 56, kKDrainRegs = 160;
+// drains (32 + 2*64 + 2*160 = 480 <= 5 * 96, the launch budget).
+constexpr int kKCtlRegs = 32, kKConvRegs = 64, kKDrainRegs = 160;
 constexpr int kKAbufs = 2;       // A buffers in TMEM (columns [384, 512)), one per converter warpgroup
 constexpr int kKAcc = 3;         // accumulators in TMEM (columns [0, 384))
 constexpr int kKHeader = 12288;  // barriers / scratch / partial-logit ring at the start of dynamic smem
@@ -196,6 +196,47 @@ __device__ __forceinline__ void convert_row_i8(const uint8_t* srow, uint32_t tad
       if constexpr (N & 1) tmem_st8(taddr + col, o + col);
     }
   }
+}
+
+// int8 row of RC <= 6 chunks converted into registers (two chunks loaded at a
+// time), and the stores of such a row (fewest wide tcgen05.st): the conversion
+// can run before the row's A buffer is free, the stores after.
+template <int RC>
+__device__ __forceinline__ void load_cvt_i8(const uint8_t* srow, uint32_t* o) {
+#pragma unroll
+  for (int c = 0; c < RC; c += 2) {
+    const uint4 w0 = *reinterpret_cast<const uint4*>(srow + 16 * c);
+    uint4 w1 = make_uint4(0u, 0u, 0u, 0u);
+    if (c + 1 < RC) w1 = *reinterpret_cast<const uint4*>(srow + 16 * (c + 1));
+    cvt8_i8(w0.x, w0.y, o + 8 * c);
+    cvt8_i8(w0.z, w0.w, o + 8 * c + 4);
+    if (c + 1 < RC) {
+      cvt8_i8(w1.x, w1.y, o + 8 * c + 8);
+      cvt8_i8(w1.z, w1.w, o + 8 * c + 12);
+    }
+  }
+}
+template <int RC>
+__device__ __forceinline__ void store_row_i8(uint32_t taddr, const uint32_t* o) {
+  int col = 0;
+#pragma unroll
+  for (; col + 32 <= 8 * RC; col += 32) tmem_st32(taddr + col, o + col);
+  if constexpr ((8 * RC) % 32 >= 16) {
+    tmem_st16(taddr + col, o + col);
+    col += 16;
+  }
+  if constexpr ((8 * RC) % 16 >= 8) tmem_st8(taddr + col, o + col);
+}
+
+// Convert, release the stage, wait for the A buffer, store: RC <= 6 int8 chunks.
+template <int RC, typename Release, typename WaitA>
+__device__ __forceinline__ bool convert_ahead_i8(const uint8_t* srow, uint32_t taddr, Release release, WaitA wait_a) {
+  uint32_t o[8 * RC];
+  load_cvt_i8<RC>(srow, o);
+  release();
+  if (!wait_a()) return false;
+  store_row_i8<RC>(taddr, o);
+  return true;
 }
 
 // Convert a staged row of rc chunks into TMEM: int8 rows in one piece, other
@@ -343,10 +384,10 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   uint64_t* st_empty = bars + 32;                // [32] unit slot read by the 4 converter warps
   uint64_t* a_full = bars + 64;                  // [2]  A buffer written (4 converter warps)
   uint64_t* a_empty = bars + 80;                 // [2]  A buffer's MMAs retired (commit)
-  uint64_t* d_full = bars + 96;                  // [6]  job slot j % 6: accumulator j % 3 ready (commit)
-  uint64_t* d_empty = bars + 102;                // [6]  job slot j % 6: accumulator read by the job's 4 drain warps
-  uint64_t* fin_bar = bars + 108;
-  uint64_t* w_bar = bars + 109;                  // W images landed (pre-pass mode)
+  uint64_t* d_full = bars + 96;                  // [6G] job slot j % 6G: accumulator j % 3 ready (commit)
+  uint64_t* d_empty = bars + 120;                // [6G] job slot j % 6G: accumulator read by the job's 4 drain warps
+  uint64_t* fin_bar = bars + 144;
+  uint64_t* w_bar = bars + 145;                  // W images landed (pre-pass mode)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 512);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 516);
   int* s_nruns = reinterpret_cast<int*>(smem + 520);
@@ -358,7 +399,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   int* s_runlen = reinterpret_cast<int*>(smem + 592);         // [4] heads in run n
   float* s_red = reinterpret_cast<float*>(smem + 704);        // [64]
   float2* s_rot = reinterpret_cast<float2*>(smem + 1024);     // [64] rotation by 128 positions
-  float4* s_rot4 = reinterpret_cast<float4*>(smem + 4096);    // [32] the same per frequency pair (cos.xy, sin.xy)
+  float4* s_rot4 = reinterpret_cast<float4*>(smem + 4096);    // [32] rotation by 256 positions per frequency pair (cos.xy, sin.xy)
   float* s_qall = reinterpret_cast<float*>(smem + 1536);      // [4][128]
   uint8_t* Bsm = smem + kKHeader;
   uint8_t* Ssm = Bsm + (size_t)p.bsum * 256;
@@ -374,7 +415,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       mbar_init(a_full + k, 4);
       mbar_init(a_empty + k, 1);
     }
-    for (int k = 0; k < 2 * kKAcc; ++k) {
+    for (int k = 0; k < 6 * G; ++k) {
       mbar_init(d_full + k, 1);
       mbar_init(d_empty + k, 4);       // the drain warpgroup of the job
     }
@@ -470,11 +511,11 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       // When every query head of the group has its own KV head (one job per unit),
       // warps 1 and 2 issue the units of parity 0 and 1 (the bookkeeping of one
       // overlaps the MMAs of the other); otherwise warp 1 issues every unit.  Job j
-      // accumulates into accumulator j % 3 and signals job slot j % 6 (one job
-      // parity per slot, so each slot's phases are waited in order by one issuer and
-      // one drain warpgroup); before reusing accumulator j % 3 the issuer waits for
-      // job j - 3 to be drained (slot (j - 3) % 6, at most one phase behind: this
-      // issuer waited for job j - 9 before it issued job j - 6).
+      // accumulates into accumulator j % 3 and signals job slot j % 6G (the jobs of
+      // one slot share their issuer and their drain warpgroup, so each slot's phases
+      // are waited in order); before reusing accumulator j % 3 the issuer waits for
+      // job j - 3 to be drained (slot (j - 3) % 6G, at most one phase behind: this
+      // issuer waited for job j - 3 - 6G before it issued job j - 6G).
       named_bar_sync(1, 512 + 96);               // W matrices built (builders + warps 1-3)
       const int NI = (NR == G) ? 2 : 1;          // issuers
       const int iw = warp - 1;
@@ -492,7 +533,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
             const int g = g0 + k, j = t * G + g;
             if (j >= kKAcc) {
               const int jp = j - kKAcc;
-              if (!mbar_wait(d_empty + jp % (2 * kKAcc), (uint32_t)((jp / (2 * kKAcc)) & 1))) { ok = false; break; }
+              if (!mbar_wait(d_empty + jp % (6 * G), (uint32_t)((jp / (6 * G)) & 1))) { ok = false; break; }
             }
             tc_fence_after();
             stamp(j, kTrMmaIssue);
@@ -501,7 +542,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
             const uint32_t d = tmem + (uint32_t)(j % kKAcc) * 128u;
             mma_f16_ts(d, a_t, bdesc, IDESC, 0u);
             for (int kk = 1; kk < (r >> 4); ++kk) mma_f16_ts(d, a_t + kk * 8, bdesc + (uint64_t)(kk * 16), IDESC, 1u);
-            mma_commit(d_full + j % (2 * kKAcc));
+            mma_commit(d_full + j % (6 * G));
           }
           mma_commit(a_empty + (u & 1));
           n += NI;
@@ -532,8 +573,13 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         s_rot[bt] = make_float2(c, sn);
       }
       named_bar_sync(2, 512);
-      if (bt < 32)                                     // rotation of the pair (2bt, 2bt + 1): cos, sin, -sin
-        s_rot4[bt] = make_float4(s_rot[2 * bt].x, s_rot[2 * bt + 1].x, s_rot[2 * bt].y, s_rot[2 * bt + 1].y);
+      if (bt >= 64 && bt < 96) {                       // rotation of the pair (2i, 2i + 1) by 256 positions: cos, sin
+        const int i = bt - 64;
+        float c0, s0, c1, s1;
+        exact_sincos(256, p.inv_freq[2 * i], c0, s0);
+        exact_sincos(256, p.inv_freq[2 * i + 1], c1, s1);
+        s_rot4[i] = make_float4(c0, c1, s0, s1);
+      }
       for (int g = 0; g < G && !p.wpre; ++g) {
         const int qh = grp * G + g;
         const float* qv = s_qall + g * 128;
@@ -566,31 +612,56 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         const int ts = t % NT, s = ts * NR + n;
         if (!mbar_wait(st_full + s, (uint32_t)((t / NT) & 1))) { fail(kDevWaitCopy); break; }
         if (ct == 0) stamp(j, kTrConvBegin);
-        if (!mbar_wait(a_empty + cw, (uint32_t)(((u >> 1) & 1) ^ 1))) { fail(kDevWaitMma); break; }
-        tc_fence_after();
-        if (ct == 0) stamp(j, kTrConvAEmpty);
         const int rc = (r * XB) >> 4;
         const uint8_t* srow = Ssm + (size_t)ts * TB + s_runoff[n] + (size_t)ct * r * XB;
-        convert_row<XT>(rc, srow, lane_base + 384u + (uint32_t)cw * 64u);
+        const uint32_t taddr = lane_base + 384u + (uint32_t)cw * 64u;
+        auto release = [&] {                       // the stage is read: hand it back to the producer
+          __syncwarp();
+          if (lane == 0) mbar_arrive(st_empty + s);
+        };
+        auto wait_a = [&]() -> bool {              // the A buffer's previous MMAs retired
+          if (!mbar_wait(a_empty + cw, (uint32_t)(((u >> 1) & 1) ^ 1))) { fail(kDevWaitMma); return false; }
+          tc_fence_after();
+          if (ct == 0) stamp(j, kTrConvAEmpty);
+          return true;
+        };
+        bool okc = true;
+        if constexpr (XB == 1) {
+          switch (rc) {
+            case 1: okc = convert_ahead_i8<1>(srow, taddr, release, wait_a); break;
+            case 2: okc = convert_ahead_i8<2>(srow, taddr, release, wait_a); break;
+            case 3: okc = convert_ahead_i8<3>(srow, taddr, release, wait_a); break;
+            case 4: okc = convert_ahead_i8<4>(srow, taddr, release, wait_a); break;
+            case 5: okc = convert_ahead_i8<5>(srow, taddr, release, wait_a); break;
+            case 6: okc = convert_ahead_i8<6>(srow, taddr, release, wait_a); break;
+            default:
+              okc = wait_a();
+              if (okc) convert_row<XT>(rc, srow, taddr);
+              release();
+              break;
+          }
+        } else {
+          okc = wait_a();
+          if (okc) convert_row<XT>(rc, srow, taddr);
+          release();
+        }
+        if (!okc) break;
         if (ct == 0) stamp(j, kTrConvPre);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(st_empty + s);
-          mbar_arrive(a_full + cw);
-        }
+        if (lane == 0) mbar_arrive(a_full + cw);
         if (ct == 0) stamp(j, kTrConvDone);
         n += 2;
         while (n >= NR) { n -= NR; ++t; }
       }
     } else {
       // ============================================================ drain warpgroups
-      // Warpgroup w = wg - 3 takes the jobs j with j % 2 == w.  Per job: thread =
-      // token row (TMEM lane) with cos / sin of all 64 frequencies at its token in
-      // registers (advanced by 128 positions per tile with packed fp32x2
-      // rotations), eight 16-column TMEM loads, packed fp32x2 FMAs, then scale,
-      // mask, the logit to HBM and the running maximum per head.
+      // Warpgroup w = wg - 3 takes every job of the tiles t with t % 2 == w.  Per
+      // job: thread = token row (TMEM lane) with cos / sin of all 64 frequencies at
+      // its token in registers (advanced by 256 positions per tile of its own with
+      // packed fp32x2 rotations), eight 16-column TMEM loads, packed fp32x2 FMAs,
+      // then scale, mask, the logit to HBM and the running maximum per head.
       regs_inc<kKDrainRegs>();
       const int w2 = wg - 3;
       const int dw = warp & 3;                           // TMEM lane quarter
@@ -598,23 +669,18 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       float2 cs_c[32], cs_s[32];                         // cos / sin of frequencies (2i, 2i+1)
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        exact_sincos(t_begin + row, p.inv_freq[2 * i], cs_c[i].x, cs_s[i].x);
-        exact_sincos(t_begin + row, p.inv_freq[2 * i + 1], cs_c[i].y, cs_s[i].y);
+        exact_sincos(t_begin + 128 * w2 + row, p.inv_freq[2 * i], cs_c[i].x, cs_s[i].x);
+        exact_sincos(t_begin + 128 * w2 + row, p.inv_freq[2 * i + 1], cs_c[i].y, cs_s[i].y);
       }
-      int cur_tile = 0;
       float m_run[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) m_run[g] = kNegBig;
       const uint32_t lbase = tmem + ((uint32_t)(dw * 32) << 16);
       float* const lg_base = p.logits + ((int64_t)b * Hq + grp * G) * p.T + t_begin + row;
       bool ok = true;
-      int ds = w2;                                       // job slot j % 6 and its phase
-      uint32_t dph = 0;
-      for (int j = w2; j < J && ok; j += 2) {
-        const int db = j % kKAcc;                        // accumulator
+      for (int tile = w2; tile < ntiles && ok; tile += 2) {
         if (*s_abort) { ok = false; break; }
-        const int tile = j / G, g = j - tile * G;
-        for (; cur_tile < tile; ++cur_tile) {            // advance every frequency by 128 positions
+        if (tile > w2) {                                 // advance every frequency by 256 positions
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const float4 r = s_rot4[i];
@@ -626,47 +692,54 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
             asm volatile("" ::: "memory");               // keep each constant's load beside its use (no hoisting)
           }
         }
-        if (row == 0) stamp(j, kTrDrainWait);
-        if (!mbar_wait(d_full + ds, dph)) { ok = false; break; }
-        tc_fence_after();
-        if (row == 0) stamp(j, kTrDrainGot);
-        const uint32_t ta = lbase + (uint32_t)db * 128u;
-        float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll 1
+        for (int g = 0; g < G; ++g) {
+          const int j = tile * G + g;
+          const int db = j % kKAcc, ds = j % (6 * G);    // accumulator, job slot
+          // the epilogue's operands first, so that their latency overlaps the waits
+          const int l = t_begin + tile * 128 + row;
+          const bool live = l < t_end;
+          const float esc = s_epi[g];
+          const float madd = (p.mask && live) ? p.mask[(int64_t)b * p.T + l] * p.mask_scale : 0.f;
+          float* const dst = lg_base + (int64_t)g * p.T + tile * 128;
+          if (row == 0) stamp(j, kTrDrainWait);
+          if (!mbar_wait(d_full + ds, (uint32_t)((j / (6 * G)) & 1))) { ok = false; break; }
+          tc_fence_after();
+          if (row == 0) stamp(j, kTrDrainGot);
+          const uint32_t ta = lbase + (uint32_t)db * 128u;
+          float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {                    // columns [16q, 16q + 16): q < 4 cosine part, else sine part
-          float v[16];
-          tmem_ld16(ta + 16u * q, v);
-          if (q == 7) {                                  // accumulator free for the MMA of job j + kKAcc
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty + ds);
-          }
-          const int f0 = (q & 3) * 8;                    // first frequency pair of this block
+          for (int q = 0; q < 8; ++q) {                  // columns [16q, 16q + 16): q < 4 cosine part, else sine part
+            float v[16];
+            tmem_ld16(ta + 16u * q, v);
+            if (q == 7) {                                // accumulator free for the MMA of job j + kKAcc
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(d_empty + ds);
+            }
+            const int f0 = (q & 3) * 8;                  // first frequency pair of this block
 #pragma unroll
-          for (int i = 0; i < 8; i += 2) {
-            if (q < 4) {
-              acc0 = __ffma2_rn(cs_c[f0 + i], make_float2(v[2 * i], v[2 * i + 1]), acc0);
-              acc1 = __ffma2_rn(cs_c[f0 + i + 1], make_float2(v[2 * i + 2], v[2 * i + 3]), acc1);
-            } else {
-              acc0 = __ffma2_rn(cs_s[f0 + i], make_float2(v[2 * i], v[2 * i + 1]), acc0);
-              acc1 = __ffma2_rn(cs_s[f0 + i + 1], make_float2(v[2 * i + 2], v[2 * i + 3]), acc1);
+            for (int i = 0; i < 8; i += 2) {
+              if (q < 4) {
+                acc0 = __ffma2_rn(cs_c[f0 + i], make_float2(v[2 * i], v[2 * i + 1]), acc0);
+                acc1 = __ffma2_rn(cs_c[f0 + i + 1], make_float2(v[2 * i + 2], v[2 * i + 3]), acc1);
+              } else {
+                acc0 = __ffma2_rn(cs_s[f0 + i], make_float2(v[2 * i], v[2 * i + 1]), acc0);
+                acc1 = __ffma2_rn(cs_s[f0 + i + 1], make_float2(v[2 * i + 2], v[2 * i + 3]), acc1);
+              }
             }
           }
-        }
-        if (row == 0) stamp(j, kTrDrainLd);
-        const float sum = (acc0.x + acc0.y) + (acc1.x + acc1.y);
-        const int l = t_begin + tile * 128 + row;
-        if (l < t_end) {
-          float val = sum * s_epi[g];
-          if (p.mask) val = fmaf(p.mask[(int64_t)b * p.T + l], p.mask_scale, val);
-          lg_base[(int64_t)g * p.T + tile * 128] = val;
+          if (row == 0) stamp(j, kTrDrainLd);
+          const float sum = (acc0.x + acc0.y) + (acc1.x + acc1.y);
+          if (live) {
+            const float val = fmaf(sum, esc, madd);
+            *dst = val;
 #pragma unroll
-          for (int gg = 0; gg < G; ++gg)
-            if (gg == g) m_run[gg] = fmaxf(m_run[gg], val);
+            for (int gg = 0; gg < G; ++gg)
+              if (gg == g) m_run[gg] = fmaxf(m_run[gg], val);
+          }
+          if (row == 0) stamp(j, kTrDrainDone);
         }
-        if (row == 0) stamp(j, kTrDrainDone);
-        ds += 2;
-        if (ds >= 2 * kKAcc) { ds -= 2 * kKAcc; dph ^= 1u; }
       }
       if (!ok) fail(kDevWaitMma);
 #pragma unroll
