@@ -338,10 +338,55 @@ __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ Co
     o_lat[c] = s * inv;
   }
   __syncthreads();
-  const int64_t urow = ((int64_t)kv * 128 + tid) * R + vcol;
-  float acc = 0.f;
-  for (int c = 0; c < r; ++c) acc = fmaf(o_lat[c], load_as_f32(p.v_u, p.w_dtype, urow + c), acc);
-  store_from_f32(p.out, p.out_dtype, ((int64_t)b * Hq + qh) * 128 + tid, acc);
+  // out[d] = sum_c o_lat[c] * U_v[kv * 128 + d, vcol + c]: warp w takes the rows
+  // d = w, w + 4, ...; lane l the 8 consecutive channels 8l + 256k of the row (one
+  // 16-byte load for 16-bit weights; its 8 latent values stay in registers), then
+  // a shuffle reduction.
+  const int warp = tid >> 5, lane = tid & 31;
+  const bool vec = p.w_dtype != STARKV_F32 && (R % 8) == 0 && (vcol % 8) == 0 && (r % 8) == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.v_u) & 15) == 0;
+  float ol[kVMaxRank / 256][8];
+#pragma unroll
+  for (int k = 0; k < kVMaxRank / 256; ++k)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = lane * 8 + 256 * k + e;
+      ol[k][e] = c < r ? o_lat[c] : 0.f;
+    }
+  for (int d = warp; d < 128; d += 4) {
+    const int64_t urow = ((int64_t)kv * 128 + d) * R + vcol;
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < kVMaxRank / 256; ++k) {
+      const int c = lane * 8 + 256 * k;
+      if (c >= r) break;
+      if (vec) {
+        const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.v_u) + urow + c);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float lo, hi;
+          if (p.w_dtype == STARKV_F16) {
+            const __half2 h = *reinterpret_cast<const __half2*>(&ws[e]);
+            lo = __low2float(h);
+            hi = __high2float(h);
+          } else {
+            lo = __uint_as_float(ws[e] << 16);
+            hi = __uint_as_float(ws[e] & 0xFFFF0000u);
+          }
+          acc = fmaf(ol[k][2 * e], lo, acc);
+          acc = fmaf(ol[k][2 * e + 1], hi, acc);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (c + e < r) acc = fmaf(ol[k][e], load_as_f32(p.v_u, p.w_dtype, urow + c + e), acc);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) store_from_f32(p.out, p.out_dtype, ((int64_t)b * Hq + qh) * 128 + d, acc);
+  }
 }
 
 // ============================================================================
