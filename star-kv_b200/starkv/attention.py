@@ -76,9 +76,9 @@ class StarKVCache:
     def layer(self, layer_idx: int, module: "LlamaCustomAttention", batch: int, dtype: torch.dtype) -> DecodeLayer:
         st = self.layers.get(layer_idx)
         if st is None:
+            v_ranks, v_kv = module.v_blocks()
             lay = ops.make_layout(batch, module.num_heads, module.num_key_value_heads, module.k_ranks(),
-                                  [module.v_rank()], [module.num_key_value_heads], self.capacity,
-                                  self.quantized, dtype)
+                                  v_ranks, v_kv, self.capacity, self.quantized, dtype)
             st = DecodeLayer(lay, module.packed_k_u(dtype), module.v_proj.U.weight.to(dtype).contiguous(),
                              module.rope_theta)
             self.layers[layer_idx] = st
@@ -118,18 +118,38 @@ class LlamaCustomAttention(nn.Module):
 
     # ---- weight views in the layouts the kernels consume
     def k_ranks(self):
+        """Per-KV-head K ranks: the reference's uniform ``k_proj.U`` ``[Hkv, 128, r]``
+        or the per-head ranks of a ``RaggedKProj`` (``starkv.export``)."""
+        ranks = getattr(self.k_proj, "ranks", None)
+        if ranks is not None:
+            return list(ranks)
         r = int(self.k_proj.U.shape[-1])
         return [r] * self.num_key_value_heads
+
+    def k_uniform(self) -> bool:
+        return len(set(self.k_ranks())) == 1
+
+    def k_u_heads(self):
+        """Per-head K up-projections ``[128, r_h]``."""
+        if hasattr(self.k_proj, "u_heads"):
+            return self.k_proj.u_heads()
+        return list(self.k_proj.U.unbind(0))
 
     def v_rank(self) -> int:
         return int(self.v_proj.U.weight.shape[1])
 
+    def v_blocks(self):
+        """V block ranks and KV heads per block (one global block in the reference)."""
+        if hasattr(self.v_proj, "kv_per_block"):
+            return list(self.v_proj.ranks), list(self.v_proj.kv_per_block)
+        return [self.v_rank()], [self.num_key_value_heads]
+
     def packed_k_u(self, dtype) -> torch.Tensor:
-        """k_proj.U as (Hkv, 128, r) contiguous == the packed per-head layout."""
-        u = self.k_proj.U
-        key = (u.data_ptr(), dtype)
+        """The per-head K up-projections in the packed layout (head after head)."""
+        heads = self.k_u_heads()
+        key = (tuple(u.data_ptr() for u in heads), dtype)
         if self._u_cache is None or self._u_cache[0] != key:
-            self._u_cache = (key, u.to(dtype).contiguous().reshape(-1))
+            self._u_cache = (key, torch.cat([u.to(dtype).contiguous().reshape(-1) for u in heads]))
         return self._u_cache[1]
 
     # ---- forward
@@ -144,6 +164,10 @@ class LlamaCustomAttention(nn.Module):
         k_lat = torch.matmul(hidden_states, self.k_proj.VS.weight.T)          # (B, q, Hkv*r)
         v_lat = torch.matmul(hidden_states, self.v_proj.VS.weight.T)          # (B, q, rv)
         r = self.k_ranks()[0]
+        uniform = self.k_uniform()
+
+        def key_view(lat):                     # (B, Hkv, L, r) for uniform ranks, else the (B, L, sum r_h) latents
+            return lat.view(B, lat.shape[1], Hkv, r).transpose(1, 2) if uniform else lat
 
         if isinstance(past_key_values, StarKVCache):
             st = past_key_values.layer(self.layer_idx, self, B, dt)
@@ -154,16 +178,20 @@ class LlamaCustomAttention(nn.Module):
             if st.length != 0:
                 raise NotImplementedError("multi-token steps after the prompt are not supported by the decode path")
             st.prefill(k_lat.contiguous(), v_lat.contiguous())
-            keys, values = k_lat.view(B, q_len, Hkv, r).transpose(1, 2), v_lat
+            keys, values = key_view(k_lat), v_lat
         elif past_key_values is not None:
+            if not uniform:
+                raise ValueError("ragged K ranks need a StarKVCache (an HF Cache stores (B, Hkv, L, r) tensors)")
             keys, values = past_key_values.update(k_lat.view(B, q_len, Hkv, r).transpose(1, 2), v_lat,
                                                   self.layer_idx)
             if q_len == 1:
                 out = self._decode_on_tensors(q[:, :, 0, :], keys, values, attention_mask)
                 return self.o_proj(out.reshape(B, 1, Hq * D)), None
         else:
-            keys, values = k_lat.view(B, q_len, Hkv, r).transpose(1, 2), v_lat
+            keys, values = key_view(k_lat), v_lat
             if q_len == 1:
+                if not uniform:
+                    raise ValueError("ragged K ranks need a StarKVCache for decode steps")
                 out = self._decode_on_tensors(q[:, :, 0, :], keys, values, attention_mask)
                 return self.o_proj(out.reshape(B, 1, Hq * D)), None
         out = self._prompt_attention(q, keys, values, cos, sin, attention_mask)
@@ -183,7 +211,8 @@ class LlamaCustomAttention(nn.Module):
         keys = keys.contiguous()
         values = values.contiguous()
         dt = keys.dtype
-        lay = ops.make_layout(B, self.num_heads, Hkv, [r] * Hkv, [values.shape[-1]], [Hkv], L, False, dt,
+        v_ranks, v_kv = self.v_blocks()
+        lay = ops.make_layout(B, self.num_heads, Hkv, [r] * Hkv, v_ranks, v_kv, L, False, dt,
                               k_offsets=[h * L * r for h in range(Hkv)], k_batch_strides=[Hkv * L * r] * Hkv)
         cache = ops.LatentCache.__new__(ops.LatentCache)
         cache.layout, cache.k_cache, cache.k_scales = lay, keys.reshape(-1), None
@@ -200,8 +229,15 @@ class LlamaCustomAttention(nn.Module):
         (model.py:429-449)."""
         B, Hq, Lq, D = q.shape
         Hkv = self.num_key_value_heads
-        u = self.k_proj.U.to(keys.dtype)                                       # (Hkv, D, r)
-        k_full = torch.matmul(keys, u.transpose(-2, -1))                       # (B, Hkv, L, D)
+        if keys.dim() == 4:                                                    # (B, Hkv, L, r)
+            u = torch.stack(self.k_u_heads()).to(keys.dtype)                   # (Hkv, D, r)
+            k_full = torch.matmul(keys, u.transpose(-2, -1))                   # (B, Hkv, L, D)
+        else:                                                                  # ragged (B, L, sum r_h)
+            cols = [0]
+            for rh in self.k_ranks():
+                cols.append(cols[-1] + rh)
+            k_full = torch.stack([torch.matmul(keys[..., cols[h]:cols[h + 1]], u.to(keys.dtype).T)
+                                  for h, u in enumerate(self.k_u_heads())], dim=1)
         k_full = apply_rotary_pos_emb_custom(k_full, cos, sin)
         v_full = torch.matmul(values, self.v_proj.U.weight.T.to(values.dtype))
         v_full = v_full.view(B, -1, Hkv, D).transpose(1, 2)
