@@ -157,7 +157,7 @@ V2Geom v2_geometry(const starkv_layout& l) {
   memset(&g, 0, sizeof(g));
   if (!l.quantized) return g;
   const int Hq = l.num_q_heads, qpk = Hq / l.num_kv_heads, R = l.v_rank_total;
-  if (Hq > kV2MaxHeads || Hq % 8) return g;
+  if (Hq > kV2MaxHeads) return g;
   (void)qpk;
   // M units are consecutive 128-channel ranges of the whole latent row; every
   // unit's MMA covers all query heads (N = np >= Hq), one shared B tile.

@@ -673,7 +673,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       s_mx[h] = m;
     }
     named_bar_sync(1, 64);
-    const int G8 = Hq >> 3;
+    const int G8 = (Hq + 7) >> 3;                  // groups of 8 heads (the last may be partial)
     // destination of this lane's (head, 8-token block) in a B tile, per head group
     int dstoff[kV2MaxHeads / 8];
     float mh[kV2MaxHeads / 8], psum[kV2MaxHeads / 8];
@@ -685,7 +685,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       if (q < G8) {
         const int g = q * 8 + (lane & 7);
         dstoff[q] = (g >> 3) * 1024 + (g & 7) * 16;
-        mh[q] = s_mx[g];
+        mh[q] = g < Hq ? s_mx[g] : 0.f;
       }
     }
     const int kb = (lane >> 3) + 4 * pw;           // 8-token block of the tile
@@ -696,7 +696,8 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         if (q < G8) {
           const float* src = p.logits + ((int64_t)b * Hq + q * 8 + (lane & 7)) * p.T + l0;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) lg[q][e] = (t < ntiles && l0 + e < t_end) ? __ldg(src + e) : kNegBig;
+          for (int e = 0; e < 8; ++e)
+            lg[q][e] = (q * 8 + (lane & 7) < Hq && t < ntiles && l0 + e < t_end) ? __ldg(src + e) : kNegBig;
         }
     };
     float lg[kV2MaxHeads / 8][8];
@@ -714,7 +715,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
           __align__(16) __half hv[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            const float x = (l0 + e < t_end) ? exp2f(lg[q][e] - mh[q]) : 0.f;
+            const float x = (q * 8 + (lane & 7) < Hq && l0 + e < t_end) ? exp2f(lg[q][e] - mh[q]) : 0.f;
             psum[q] += x;
             hv[e] = __float2half_rn(x * kVPScale);
           }

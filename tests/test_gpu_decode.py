@@ -67,7 +67,7 @@ def test_decode_matches_reference_golden(cuda, name):
     ("c1", dict(num_q_heads=8, batch=2, context=127), False),     # T = 128 exactly
     ("c1", dict(num_q_heads=8, batch=2, context=128), False),     # T = 129 (one-row tail)
     ("c1", dict(num_q_heads=4, batch=1, context=1), False),       # T = 2
-    ("c1", dict(num_q_heads=12, batch=2, context=900), False),    # 12 heads: the per-block V kernel
+    ("c1", dict(num_q_heads=12, batch=2, context=900), False),    # 12 heads: a partial group of 8 in the V prob warps
     ("c1", dict(num_q_heads=32, batch=3, context=1500), True),
     ("c2", dict(num_q_heads=32, num_kv_heads=8, batch=2, context=2000), False),
     ("c0", dict(num_q_heads=8, batch=2, context=700, dtype="float16"), False),
