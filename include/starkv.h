@@ -122,6 +122,22 @@ int starkv_append(const starkv_layout* lay, const void* k_lat, const void* v_lat
                   int32_t num_tokens, int32_t start_slot, void* k_cache, const void* k_scales,
                   void* v_cache, void* v_params, starkv_stream_t stream);
 
+/*
+ * Fused latent projection + quantise-append of one decode token per sequence:
+ * k_lat = hidden @ vs_k^T, v_lat = hidden @ vs_v^T (fp32 dot products rounded to
+ * the latent dtype), then the same quantiser / append as starkv_append at `slot`.
+ * Replaces the k_proj.VS / v_proj.VS projections and the cache update of
+ * LlamaLoRaAttention_headwise.py:86-99 (LlamaLoRaAttention_headwise_quant.py:94-127).
+ * hidden: (batch, hidden_size); vs_k: (k_rank_total, hidden_size) (the heads'
+ * rows concatenated); vs_v: (v_rank_total, hidden_size); all in the latent dtype,
+ * 16-byte aligned rows.  k_lat_out / v_lat_out (nullable): (batch, k_rank_total) /
+ * (batch, v_rank_total) receive the rounded latents.
+ */
+int starkv_project_append(const starkv_layout* lay, const void* hidden, int32_t hidden_size,
+                          const void* vs_k, const void* vs_v, int32_t slot, void* k_cache,
+                          const void* k_scales, void* v_cache, void* v_params, void* k_lat_out,
+                          void* v_lat_out, starkv_stream_t stream);
+
 typedef struct starkv_decode_args {
   const void* q;            /* (B, Hq, 128) rotated query, q_dtype, contiguous */
   int32_t q_dtype;

@@ -139,3 +139,120 @@ __global__ void __launch_bounds__(256) copy_append_kernel(const starkv_layout la
 }
 
 }  // namespace starkv
+
+namespace starkv {
+
+// ---- fused latent projection + quantise-append of one decode token per sequence
+// (the reference's k_proj.VS / v_proj.VS GEMVs, headwise.py:86-96, followed by the
+// cache append, headwise.py:99 / quant.py:107-127).  Channel space: the K latents
+// (sum r_h, heads concatenated) then the V latents (R).  One warp per chunk of 32
+// channels (V chunks are the quantiser's groups of 32): for every channel of the
+// chunk the warp reads its VS row once, 16 bytes a lane (coalesced), dots it with
+// every sequence's hidden state (staged in shared memory for kPaSeq sequences at a
+// time) and reduces with shuffles.  The fp32 dot is rounded to the latent type
+// (the reference's projection output) and quantised exactly as the append
+// kernels do; k_out / v_out optionally receive the rounded latents.
+constexpr int kPaWarps = 8;
+constexpr int kPaSeq = 8;          // sequences per pass (one register accumulator each)
+
+template <typename LT, bool QUANT>
+__global__ void __launch_bounds__(kPaWarps * 32) project_append_kernel(
+    const starkv_layout lay, const LT* __restrict__ hidden, int H, const LT* __restrict__ vs_k,
+    const LT* __restrict__ vs_v, int slot, void* __restrict__ k_cache, const __half* __restrict__ k_scales,
+    void* __restrict__ v_cache, __half2* __restrict__ v_params, LT* __restrict__ k_out, LT* __restrict__ v_out) {
+  extern __shared__ __align__(16) uint8_t pa_smem[];
+  LT* hs = reinterpret_cast<LT*>(pa_smem);                      // [kPaSeq][H]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = lay.k_rank_total, R = lay.v_rank_total;
+  const int kchunks = (K + 31) / 32, nchunks = kchunks + R / 32;
+  const int chunk = blockIdx.x * kPaWarps + warp;
+  constexpr int VEC = 16 / (int)sizeof(LT);                     // elements per 16-byte load
+  for (int b0 = 0; b0 < lay.batch; b0 += kPaSeq) {
+    const int nb = min(kPaSeq, lay.batch - b0);
+    __syncthreads();
+    for (int e = threadIdx.x * VEC; e < nb * H; e += blockDim.x * VEC)
+      *reinterpret_cast<uint4*>(hs + e) = *reinterpret_cast<const uint4*>(hidden + (int64_t)b0 * H + e);
+    __syncthreads();
+    if (chunk >= nchunks) continue;
+    const bool isk = chunk < kchunks;
+    const int c0 = isk ? chunk * 32 : (chunk - kchunks) * 32;
+    const int nc = isk ? min(32, K - c0) : 32;
+    float mine[kPaSeq];                                         // lane = channel c0 + lane: its latent per sequence
+#pragma unroll
+    for (int s = 0; s < kPaSeq; ++s) mine[s] = 0.f;
+    for (int c = 0; c < nc; ++c) {
+      const LT* row = (isk ? vs_k : vs_v) + (int64_t)(c0 + c) * H;
+      float acc[kPaSeq];
+#pragma unroll
+      for (int s = 0; s < kPaSeq; ++s) acc[s] = 0.f;
+      for (int k = lane * VEC; k < H; k += 32 * VEC) {
+        const uint4 w = *reinterpret_cast<const uint4*>(row + k);
+        const LT* wv = reinterpret_cast<const LT*>(&w);
+#pragma unroll
+        for (int s = 0; s < kPaSeq; ++s)
+          if (s < nb) {
+            const uint4 x = *reinterpret_cast<const uint4*>(hs + s * H + k);
+            const LT* xv = reinterpret_cast<const LT*>(&x);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) acc[s] = fmaf(to_f32(xv[e]), to_f32(wv[e]), acc[s]);
+          }
+      }
+#pragma unroll
+      for (int s = 0; s < kPaSeq; ++s) {
+        float a = acc[s];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == c) mine[s] = a;
+      }
+    }
+    // round to the latent type, then store / quantise (lane = channel c0 + lane)
+    for (int s = 0; s < nb; ++s) {
+      const int b = b0 + s;
+      const LT lat = from_f32<LT>(mine[s]);
+      const float x = to_f32(lat);
+      if (isk) {
+        if (lane < nc) {
+          const int ch = c0 + lane;
+          int kv = 0;
+          while (kv + 1 < lay.num_kv_heads && lay.k_col[kv + 1] <= ch) ++kv;
+          const int c = ch - lay.k_col[kv], r = lay.k_rank[kv];
+          const int64_t dst = lay.k_offset[kv] + (int64_t)b * lay.k_batch_stride[kv] + (int64_t)slot * r + c;
+          if (k_out) k_out[(int64_t)b * K + ch] = lat;
+          if constexpr (QUANT) {
+            const float sc = __half2float(k_scales[(int64_t)b * K + ch]);
+            float q = rintf(__fdiv_rn(x, sc));
+            q = fminf(fmaxf(q, -127.f), 127.f);
+            reinterpret_cast<int8_t*>(k_cache)[dst] = (int8_t)(int)q;
+          } else {
+            reinterpret_cast<LT*>(k_cache)[dst] = lat;
+          }
+        }
+      } else {
+        const int64_t rowi = (int64_t)b * lay.capacity + slot;
+        if (v_out) v_out[(int64_t)b * R + c0 + lane] = lat;
+        if constexpr (QUANT) {
+          float mn = x, mx = x;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) {
+            mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+          }
+          __half hsc = __float2half_rn(__fdiv_rn(__fsub_rn(mx, mn), 15.0f));
+          if (__half2float(hsc) == 0.0f) hsc = __float2half_rn(1.0f);
+          const __half hz = __float2half_rn(mn);
+          float q = rintf(__fdiv_rn(__fsub_rn(x, __half2float(hz)), __half2float(hsc)));
+          q = fminf(fmaxf(q, 0.f), 15.f);
+          const uint32_t qi = (uint32_t)(int)q;
+          const uint32_t hi = __shfl_down_sync(0xffffffffu, qi, 1);
+          if ((lane & 1) == 0)
+            reinterpret_cast<uint8_t*>(v_cache)[rowi * (R / 2) + c0 / 2 + (lane >> 1)] = (uint8_t)(qi | (hi << 4));
+          if (lane == 0) v_params[rowi * (R / 32) + c0 / 32] = __halves2half2(hsc, hz);
+        } else {
+          reinterpret_cast<LT*>(v_cache)[rowi * R + c0 + lane] = lat;
+        }
+      }
+    }
+  }
+}
+
+}  // namespace starkv

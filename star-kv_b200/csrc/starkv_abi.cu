@@ -362,6 +362,22 @@ int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp
   return STARKV_OK;
 }
 
+template <typename LT, bool QUANT>
+int launch_pa(const starkv_layout& l, const void* hidden, int H, const void* vs_k, const void* vs_v, int slot,
+              void* k_cache, const void* k_scales, void* v_cache, void* v_params, void* k_out, void* v_out,
+              cudaStream_t st) {
+  auto kern = project_append_kernel<LT, QUANT>;
+  const size_t smem = (size_t)kPaSeq * H * sizeof(LT);
+  const int slotid = 18 + 2 * (sizeof(LT) == 4 ? 0 : std::is_same<LT, __half>::value ? 1 : 2) + (QUANT ? 1 : 0);
+  int rc = ensure_smem(kern, smem, slotid > 23 ? 23 : slotid);
+  if (rc) return rc;
+  const int nchunks = (l.k_rank_total + 31) / 32 + l.v_rank_total / 32;
+  kern<<<(nchunks + kPaWarps - 1) / kPaWarps, kPaWarps * 32, smem, st>>>(
+      l, (const LT*)hidden, H, (const LT*)vs_k, (const LT*)vs_v, slot, k_cache, (const __half*)k_scales, v_cache,
+      (__half2*)v_params, (LT*)k_out, (LT*)v_out);
+  return fail_launch();
+}
+
 }  // namespace
 
 extern "C" {
@@ -376,6 +392,37 @@ int32_t starkv_auto_splits(const starkv_layout* lay, int32_t num_tokens) {
   if (validate(lay)) return 1;
   const int sms = device_sm_count(nullptr);
   return auto_splits(*lay, num_tokens, sms > 0 ? sms : 148);
+}
+
+int starkv_project_append(const starkv_layout* lay, const void* hidden, int32_t hidden_size, const void* vs_k,
+                          const void* vs_v, int32_t slot, void* k_cache, const void* k_scales, void* v_cache,
+                          void* v_params, void* k_lat_out, void* v_lat_out, starkv_stream_t stream) {
+  int rc = validate(lay);
+  if (rc) return rc;
+  const starkv_layout& l = *lay;
+  const int eb = dtype_bytes(l.latent_dtype);
+  if (!hidden || !vs_k || !vs_v || !k_cache || !v_cache || slot < 0 || slot >= l.capacity || hidden_size <= 0)
+    return set_error(STARKV_ERR_INVALID, "bad arguments (slot beyond capacity?)");
+  if (l.quantized && (!k_scales || !v_params)) return set_error(STARKV_ERR_INVALID, "null scales");
+  if ((hidden_size * eb) % 16 || (reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(vs_k) |
+                                  reinterpret_cast<uintptr_t>(vs_v)) % 16)
+    return set_error(STARKV_ERR_INVALID, "hidden rows and VS matrices must be 16-byte aligned");
+  if ((size_t)kPaSeq * hidden_size * eb > (size_t)kKSmemMax)
+    return set_error(STARKV_ERR_UNSUPPORTED, "hidden size too large for the fused projection");
+  rc = check_device();
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (l.latent_dtype) {
+    case STARKV_F16:
+      return l.quantized ? launch_pa<__half, true>(l, hidden, hidden_size, vs_k, vs_v, slot, k_cache, k_scales, v_cache, v_params, k_lat_out, v_lat_out, st)
+                         : launch_pa<__half, false>(l, hidden, hidden_size, vs_k, vs_v, slot, k_cache, k_scales, v_cache, v_params, k_lat_out, v_lat_out, st);
+    case STARKV_BF16:
+      return l.quantized ? launch_pa<__nv_bfloat16, true>(l, hidden, hidden_size, vs_k, vs_v, slot, k_cache, k_scales, v_cache, v_params, k_lat_out, v_lat_out, st)
+                         : launch_pa<__nv_bfloat16, false>(l, hidden, hidden_size, vs_k, vs_v, slot, k_cache, k_scales, v_cache, v_params, k_lat_out, v_lat_out, st);
+    default:
+      return l.quantized ? launch_pa<float, true>(l, hidden, hidden_size, vs_k, vs_v, slot, k_cache, k_scales, v_cache, v_params, k_lat_out, v_lat_out, st)
+                         : launch_pa<float, false>(l, hidden, hidden_size, vs_k, vs_v, slot, k_cache, k_scales, v_cache, v_params, k_lat_out, v_lat_out, st);
+  }
 }
 
 int starkv_decode_workspace_size(const starkv_layout* lay, int32_t num_tokens, int32_t num_splits, size_t* bytes) {

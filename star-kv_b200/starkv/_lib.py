@@ -58,6 +58,9 @@ SIGNATURES = [
                                           C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("starkv_append", C.c_int, [C.POINTER(Layout), C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_void_p,
                                 C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("starkv_project_append", C.c_int, [C.POINTER(Layout), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_int32,
+                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                        C.c_void_p]),
     ("starkv_decode_workspace_size", C.c_int, [C.POINTER(Layout), C.c_int32, C.c_int32, C.POINTER(C.c_size_t)]),
     ("starkv_auto_splits", C.c_int32, [C.POINTER(Layout), C.c_int32]),
     ("starkv_decode_attention", C.c_int, [C.POINTER(Layout), C.POINTER(DecodeArgs), C.c_void_p]),

@@ -161,8 +161,10 @@ class LlamaCustomAttention(nn.Module):
         q = self.q_proj(hidden_states).view(B, q_len, Hq, D).transpose(1, 2)
         cos, sin = position_embeddings
         q = apply_rotary_pos_emb_custom(q, cos, sin)
-        k_lat = torch.matmul(hidden_states, self.k_proj.VS.weight.T)          # (B, q, Hkv*r)
-        v_lat = torch.matmul(hidden_states, self.v_proj.VS.weight.T)          # (B, q, rv)
+        fused_decode = isinstance(past_key_values, StarKVCache) and q_len == 1
+        if not fused_decode:
+            k_lat = torch.matmul(hidden_states, self.k_proj.VS.weight.T)      # (B, q, Hkv*r)
+            v_lat = torch.matmul(hidden_states, self.v_proj.VS.weight.T)      # (B, q, rv)
         r = self.k_ranks()[0]
         uniform = self.k_uniform()
 
@@ -173,7 +175,9 @@ class LlamaCustomAttention(nn.Module):
             st = past_key_values.layer(self.layer_idx, self, B, dt)
             if q_len == 1:
                 mask = self._decode_mask(attention_mask, B, st.length + 1)
-                out = st.step(q[:, :, 0, :], k_lat.contiguous(), v_lat.contiguous(), mask=mask)
+                # fused k_proj.VS / v_proj.VS projection + quantise-append (one kernel)
+                out = st.step_from_hidden(q[:, :, 0, :], hidden_states, self.k_proj.VS.weight.to(dt),
+                                          self.v_proj.VS.weight.to(dt), mask=mask)
                 return self.o_proj(out.reshape(B, 1, Hq * D)), None
             if st.length != 0:
                 raise NotImplementedError("multi-token steps after the prompt are not supported by the decode path")

@@ -57,6 +57,14 @@ class DecodeLayer:
                                     self.inv_freq, self.scaling, T, mask=None if mask is None else mask.contiguous(), out=out,
                                     num_splits=self.num_splits, events=events)
 
+    def step_from_hidden(self, q_rot: torch.Tensor, hidden: torch.Tensor, vs_k: torch.Tensor, vs_v: torch.Tensor,
+                         mask: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                         events=None) -> torch.Tensor:
+        """Decode step from the token's hidden state: fused latent projection +
+        quantise-append (``starkv_project_append``), then attend."""
+        self.cache.project_append(hidden.contiguous(), vs_k.contiguous(), vs_v.contiguous())
+        return self.attend(q_rot, mask=mask, out=out, events=events)
+
     def step(self, q_rot: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
              mask: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
              events=None) -> torch.Tensor:

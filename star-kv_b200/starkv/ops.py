@@ -146,6 +146,30 @@ class LatentCache:
               "starkv_append")
         self.length += T
 
+    def project_append(self, hidden: torch.Tensor, vs_k: torch.Tensor, vs_v: torch.Tensor,
+                       return_latents: bool = False):
+        """One decode token per sequence straight from the hidden state: the fused
+        ``k_proj.VS`` / ``v_proj.VS`` projection + quantise-append at slot ``length``
+        (``starkv_project_append``).  hidden (B, 1, hidden) or (B, hidden); vs_k
+        (sum r_h, hidden); vs_v (R, hidden); all in the latent dtype.  With
+        ``return_latents`` the rounded latents (B, 1, sum r_h) / (B, 1, R) are returned."""
+        L = self.layout
+        H = hidden.shape[-1]
+        dt = self.latent_dtype
+        _require(hidden, "hidden", dt, L.batch * H)
+        _require(vs_k, "vs_k", dt, L.k_rank_total * H)
+        _require(vs_v, "vs_v", dt, L.v_rank_total * H)
+        k_out = v_out = None
+        if return_latents:
+            k_out = torch.empty(L.batch, 1, L.k_rank_total, dtype=dt, device=hidden.device)
+            v_out = torch.empty(L.batch, 1, L.v_rank_total, dtype=dt, device=hidden.device)
+        check(load().starkv_project_append(C.byref(L), _ptr(hidden), H, _ptr(vs_k), _ptr(vs_v), self.length,
+                                           _ptr(self.k_cache), _ptr(self.k_scales), _ptr(self.v_cache),
+                                           _ptr(self.v_params), _ptr(k_out), _ptr(v_out), _stream()),
+              "starkv_project_append")
+        self.length += 1
+        return (k_out, v_out) if return_latents else None
+
     # ---- host views for tests / export
     def k_head(self, h: int) -> torch.Tensor:
         """(B, capacity, r_h) view of KV head h."""
