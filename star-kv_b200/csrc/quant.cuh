@@ -145,15 +145,18 @@ namespace starkv {
 // ---- fused latent projection + quantise-append of one decode token per sequence
 // (the reference's k_proj.VS / v_proj.VS GEMVs, headwise.py:86-96, followed by the
 // cache append, headwise.py:99 / quant.py:107-127).  Channel space: the K latents
-// (sum r_h, heads concatenated) then the V latents (R).  One warp per chunk of 32
-// channels (V chunks are the quantiser's groups of 32): for every channel of the
-// chunk the warp reads its VS row once, 16 bytes a lane (coalesced), dots it with
-// every sequence's hidden state (staged in shared memory for kPaSeq sequences at a
-// time) and reduces with shuffles.  The fp32 dot is rounded to the latent type
-// (the reference's projection output) and quantised exactly as the append
-// kernels do; k_out / v_out optionally receive the rounded latents.
+// (sum r_h, heads concatenated) then the V latents (R).  One CTA per chunk of 32
+// channels (V chunks are the quantiser's groups of 32); its 8 warps split the
+// hidden dimension: for every channel of the chunk a warp reads its share of the
+// VS row, 16 bytes a lane (coalesced), dots it with every sequence's hidden state
+// (staged in shared memory; grid.y = passes of 8 sequences) and reduces with
+// shuffles; warp 0 adds the 8 partial sums, rounds to the latent type (the
+// reference's projection output) and quantises exactly as the append kernels do;
+// k_out / v_out optionally receive the rounded latents.
 constexpr int kPaWarps = 8;
-constexpr int kPaSeq = 8;          // sequences per pass (one register accumulator each)
+constexpr int kPaSeq = 8;          // sequences per CTA (grid.y = batch passes)
+template <typename LT>
+__host__ __device__ constexpr int kPaSeqOf() { return 8; }
 
 template <typename LT, bool QUANT>
 __global__ void __launch_bounds__(kPaWarps * 32) project_append_kernel(
@@ -161,49 +164,82 @@ __global__ void __launch_bounds__(kPaWarps * 32) project_append_kernel(
     const LT* __restrict__ vs_v, int slot, void* __restrict__ k_cache, const __half* __restrict__ k_scales,
     void* __restrict__ v_cache, __half2* __restrict__ v_params, LT* __restrict__ k_out, LT* __restrict__ v_out) {
   extern __shared__ __align__(16) uint8_t pa_smem[];
-  LT* hs = reinterpret_cast<LT*>(pa_smem);                      // [kPaSeq][H]
+  LT* hs = reinterpret_cast<LT*>(pa_smem);                      // [PS][H]
+  constexpr int PS = kPaSeqOf<LT>();                            // sequences per pass
+  __shared__ float red[kPaWarps][32][PS];                       // per-warp partial dots
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = lay.k_rank_total, R = lay.v_rank_total;
-  const int kchunks = (K + 31) / 32, nchunks = kchunks + R / 32;
-  const int chunk = blockIdx.x * kPaWarps + warp;
+  const int kchunks = (K + 31) / 32;
+  const int chunk = blockIdx.x;
+  const bool isk = chunk < kchunks;
+  const int c0 = isk ? chunk * 32 : (chunk - kchunks) * 32;
+  const int nc = isk ? min(32, K - c0) : 32;
   constexpr int VEC = 16 / (int)sizeof(LT);                     // elements per 16-byte load
-  for (int b0 = 0; b0 < lay.batch; b0 += kPaSeq) {
-    const int nb = min(kPaSeq, lay.batch - b0);
+  if (threadIdx.x < nc)                                         // the chunk's VS rows into L2 (their loads below are serial)
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((isk ? vs_k : vs_v) + (int64_t)(c0 + threadIdx.x) * H),
+                 "r"((uint32_t)(H * sizeof(LT))) : "memory");
+  {
+    const int b0 = blockIdx.y * PS;
+    const int nb = min(PS, lay.batch - b0);
     __syncthreads();
     for (int e = threadIdx.x * VEC; e < nb * H; e += blockDim.x * VEC)
       *reinterpret_cast<uint4*>(hs + e) = *reinterpret_cast<const uint4*>(hidden + (int64_t)b0 * H + e);
     __syncthreads();
-    if (chunk >= nchunks) continue;
-    const bool isk = chunk < kchunks;
-    const int c0 = isk ? chunk * 32 : (chunk - kchunks) * 32;
-    const int nc = isk ? min(32, K - c0) : 32;
-    float mine[kPaSeq];                                         // lane = channel c0 + lane: its latent per sequence
-#pragma unroll
-    for (int s = 0; s < kPaSeq; ++s) mine[s] = 0.f;
-    for (int c = 0; c < nc; ++c) {
+    for (int c = 0; c < nc; c += 4) {                           // 4 channels at a time: their loads in flight together
       const LT* row = (isk ? vs_k : vs_v) + (int64_t)(c0 + c) * H;
-      float acc[kPaSeq];
+      float acc[4][PS];
 #pragma unroll
-      for (int s = 0; s < kPaSeq; ++s) acc[s] = 0.f;
-      for (int k = lane * VEC; k < H; k += 32 * VEC) {
-        const uint4 w = *reinterpret_cast<const uint4*>(row + k);
-        const LT* wv = reinterpret_cast<const LT*>(&w);
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int s = 0; s < kPaSeq; ++s)
+        for (int s = 0; s < PS; ++s) acc[j][s] = 0.f;
+#pragma unroll 2
+      for (int k = (warp * 32 + lane) * VEC; k < H; k += kPaWarps * 32 * VEC) {
+        uint4 w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const uint4*>(row + (int64_t)j * H + k);
+        float wf[4][VEC];                                       // converted once, used for every sequence
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) wf[j][e] = to_f32(reinterpret_cast<const LT*>(&w[j])[e]);
+#pragma unroll
+        for (int s = 0; s < PS; ++s)
           if (s < nb) {
             const uint4 x = *reinterpret_cast<const uint4*>(hs + s * H + k);
             const LT* xv = reinterpret_cast<const LT*>(&x);
+            float2 a01 = make_float2(acc[0][s], acc[1][s]), a23 = make_float2(acc[2][s], acc[3][s]);
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) acc[s] = fmaf(to_f32(xv[e]), to_f32(wv[e]), acc[s]);
+            for (int e = 0; e < VEC; ++e) {                     // two channels per packed fp32x2 FMA
+              const float xf = to_f32(xv[e]);
+              a01 = __ffma2_rn(make_float2(xf, xf), make_float2(wf[0][e], wf[1][e]), a01);
+              a23 = __ffma2_rn(make_float2(xf, xf), make_float2(wf[2][e], wf[3][e]), a23);
+            }
+            acc[0][s] = a01.x;
+            acc[1][s] = a01.y;
+            acc[2][s] = a23.x;
+            acc[3][s] = a23.y;
           }
       }
 #pragma unroll
-      for (int s = 0; s < kPaSeq; ++s) {
-        float a = acc[s];
+      for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == c) mine[s] = a;
-      }
+        for (int s = 0; s < PS; ++s) {
+          float a = acc[j][s];
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+          if (lane == 0) red[warp][c + j][s] = a;
+        }
+    }
+    __syncthreads();
+    if (warp != 0) return;                                      // no barrier follows
+    float mine[PS];                                             // lane = channel c0 + lane: its latent per sequence
+#pragma unroll
+    for (int s = 0; s < PS; ++s) {
+      float a = 0.f;
+      if (lane < nc)
+#pragma unroll
+        for (int w = 0; w < kPaWarps; ++w) a += red[w][lane][s];
+      mine[s] = a;
     }
     // round to the latent type, then store / quantise (lane = channel c0 + lane)
     for (int s = 0; s < nb; ++s) {

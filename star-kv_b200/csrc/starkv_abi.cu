@@ -367,12 +367,12 @@ int launch_pa(const starkv_layout& l, const void* hidden, int H, const void* vs_
               void* k_cache, const void* k_scales, void* v_cache, void* v_params, void* k_out, void* v_out,
               cudaStream_t st) {
   auto kern = project_append_kernel<LT, QUANT>;
-  const size_t smem = (size_t)kPaSeq * H * sizeof(LT);
+  const size_t smem = (size_t)kPaSeqOf<LT>() * H * sizeof(LT);
   const int slotid = 18 + 2 * (sizeof(LT) == 4 ? 0 : std::is_same<LT, __half>::value ? 1 : 2) + (QUANT ? 1 : 0);
   int rc = ensure_smem(kern, smem, slotid > 23 ? 23 : slotid);
   if (rc) return rc;
   const int nchunks = (l.k_rank_total + 31) / 32 + l.v_rank_total / 32;
-  kern<<<(nchunks + kPaWarps - 1) / kPaWarps, kPaWarps * 32, smem, st>>>(
+  kern<<<dim3(nchunks, (l.batch + kPaSeqOf<LT>() - 1) / kPaSeqOf<LT>()), kPaWarps * 32, smem, st>>>(
       l, (const LT*)hidden, H, (const LT*)vs_k, (const LT*)vs_v, slot, k_cache, (const __half*)k_scales, v_cache,
       (__half2*)v_params, (LT*)k_out, (LT*)v_out);
   return fail_launch();
@@ -407,7 +407,7 @@ int starkv_project_append(const starkv_layout* lay, const void* hidden, int32_t 
   if ((hidden_size * eb) % 16 || (reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(vs_k) |
                                   reinterpret_cast<uintptr_t>(vs_v)) % 16)
     return set_error(STARKV_ERR_INVALID, "hidden rows and VS matrices must be 16-byte aligned");
-  if ((size_t)kPaSeq * hidden_size * eb > (size_t)kKSmemMax)
+  if ((size_t)8 * hidden_size * eb > (size_t)kKSmemMax - 32 * 1024)
     return set_error(STARKV_ERR_UNSUPPORTED, "hidden size too large for the fused projection");
   rc = check_device();
   if (rc) return rc;
