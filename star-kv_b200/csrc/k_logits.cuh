@@ -460,7 +460,6 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   const int NT = s_ring[0];                      // tile slots in the ring
   const int TB = s_ring[1];                      // bytes per tile slot
   const int U = ntiles * NR;                     // units of this CTA
-  const int J = ntiles * G;                      // jobs of this CTA
 
   long long* trace = (p.trace && split == 0 && grp == 0 && b < 2) ? p.trace + (int64_t)b * p.trace_jobs * kTrFields
                                                                   : nullptr;
