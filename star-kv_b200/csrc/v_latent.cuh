@@ -334,6 +334,7 @@ __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ Co
   for (int c = tid; c < r; c += 128) {
     float s = 0.f;
     const float* src = p.partial + ((int64_t)b * Hq + qh) * p.nsplit * p.rv_max + c;
+#pragma unroll 4
     for (int k = 0; k < p.nsplit; ++k) s += src[(int64_t)k * p.rv_max];
     o_lat[c] = s * inv;
   }
@@ -353,39 +354,54 @@ __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ Co
       const int c = lane * 8 + 256 * k + e;
       ol[k][e] = c < r ? o_lat[c] : 0.f;
     }
-  for (int d = warp; d < 128; d += 4) {
-    const int64_t urow = ((int64_t)kv * 128 + d) * R + vcol;
-    float acc = 0.f;
+  // four rows per iteration (d, d + 4, d + 8, d + 12): their loads in flight together
+  for (int d0 = warp; d0 < 128; d0 += 16) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int k = 0; k < kVMaxRank / 256; ++k) {
       const int c = lane * 8 + 256 * k;
       if (c >= r) break;
       if (vec) {
-        const uint4 w = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.v_u) + urow + c);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        uint4 w[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float lo, hi;
-          if (p.w_dtype == STARKV_F16) {
-            const __half2 h = *reinterpret_cast<const __half2*>(&ws[e]);
-            lo = __low2float(h);
-            hi = __high2float(h);
-          } else {
-            lo = __uint_as_float(ws[e] << 16);
-            hi = __uint_as_float(ws[e] & 0xFFFF0000u);
+        for (int q = 0; q < 4; ++q)
+          w[q] = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.v_u) +
+                                                 ((int64_t)kv * 128 + d0 + 4 * q) * R + vcol + c);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t ws[4] = {w[q].x, w[q].y, w[q].z, w[q].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float lo, hi;
+            if (p.w_dtype == STARKV_F16) {
+              const __half2 h = *reinterpret_cast<const __half2*>(&ws[e]);
+              lo = __low2float(h);
+              hi = __high2float(h);
+            } else {
+              lo = __uint_as_float(ws[e] << 16);
+              hi = __uint_as_float(ws[e] & 0xFFFF0000u);
+            }
+            acc[q] = fmaf(ol[k][2 * e], lo, acc[q]);
+            acc[q] = fmaf(ol[k][2 * e + 1], hi, acc[q]);
           }
-          acc = fmaf(ol[k][2 * e], lo, acc);
-          acc = fmaf(ol[k][2 * e + 1], hi, acc);
         }
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          if (c + e < r) acc = fmaf(ol[k][e], load_as_f32(p.v_u, p.w_dtype, urow + c + e), acc);
+        for (int q = 0; q < 4; ++q) {
+          const int64_t urow = ((int64_t)kv * 128 + d0 + 4 * q) * R + vcol;
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (c + e < r) acc[q] = fmaf(ol[k][e], load_as_f32(p.v_u, p.w_dtype, urow + c + e), acc[q]);
+        }
       }
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) store_from_f32(p.out, p.out_dtype, ((int64_t)b * Hq + qh) * 128 + d, acc);
+    for (int q = 0; q < 4; ++q) {
+      float a = acc[q];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) store_from_f32(p.out, p.out_dtype, ((int64_t)b * Hq + qh) * 128 + d0 + 4 * q, a);
+    }
   }
 }
 
