@@ -282,6 +282,32 @@ __device__ __forceinline__ void exact_sincos(int l, float w, float& c, float& s)
   __sincosf((float)red, &s, &c);
 }
 
+// Elements [i, i + 8) of a dtype-tagged array as float: one 16-byte load for
+// 16-bit types when the address is 16-byte aligned, else element by element.
+__device__ __forceinline__ void load8_as_f32(const void* p, int dtype, int64_t i, float* out) {
+  if (dtype != STARKV_F32) {
+    const uint16_t* q = reinterpret_cast<const uint16_t*>(p) + i;
+    if ((reinterpret_cast<uintptr_t>(q) & 15) == 0) {
+      const uint4 w = *reinterpret_cast<const uint4*>(q);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (dtype == STARKV_F16) {
+          const __half2 h = *reinterpret_cast<const __half2*>(&ws[e]);
+          out[2 * e] = __low2float(h);
+          out[2 * e + 1] = __high2float(h);
+        } else {
+          out[2 * e] = __uint_as_float(ws[e] << 16);
+          out[2 * e + 1] = __uint_as_float(ws[e] & 0xFFFF0000u);
+        }
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) out[e] = load_as_f32(p, dtype, i + e);
+}
+
 // Build W_h = [P | Q] of query head qh for sequence b (fp16, canonical no-swizzle
 // K-major layout: row n of W^T, n < 64 -> P, else Q) into Bg, by NT threads
 // (thread index t); red holds NT / 32 floats; bar() synchronises the NT threads.
@@ -306,12 +332,14 @@ __device__ __forceinline__ void build_w_head(const KParams& p, int b, int qh, co
     if (e < nch) {
       const int i = e / nc, kc = e - i * nc;
       const float qa = qv[i], qb = qv[i + 64];
+      float u1v[8], u2v[8], scv[8];                       // 8 consecutive channels: 16-byte loads where possible
+      load8_as_f32(p.k_u, p.w_dtype, ubase + (int64_t)i * r + kc * 8, u1v);
+      load8_as_f32(p.k_u, p.w_dtype, ubase + (int64_t)(i + 64) * r + kc * 8, u2v);
+      if (QUANT) load8_as_f32(scp, STARKV_F16, kc * 8, scv);
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
-        const int c = kc * 8 + cc;
-        const float u1 = load_as_f32(p.k_u, p.w_dtype, ubase + (int64_t)i * r + c);
-        const float u2 = load_as_f32(p.k_u, p.w_dtype, ubase + (int64_t)(i + 64) * r + c);
-        const float sc = QUANT ? __half2float(scp[c]) : 1.f;
+        const float u1 = u1v[cc], u2 = u2v[cc];
+        const float sc = QUANT ? scv[cc] : 1.f;
         pv[k][cc] = sc * (qa * u1 + qb * u2);
         qq[k][cc] = sc * (qb * u1 - qa * u2);
         amax = fmaxf(amax, fmaxf(fabsf(pv[k][cc]), fabsf(qq[k][cc])));
