@@ -15,39 +15,35 @@
 // TMEM drain.  The query is folded into W once per CTA, so neither the keys
 // nor the rotated keys are ever materialised.
 //
-// CTA = (sequence split, group of G query heads, sequence b), 512 threads, one
+// CTA = (sequence split, group of G query heads, sequence b), 640 threads, one
 // CTA per SM (it owns the 512 TMEM columns).  A "unit" is one 128-token tile of
 // one KV head (the G heads form runs of heads that share a KV head); a "job" is
-// one (tile, query head) pair.  Roles, handing off through mbarriers:
-//   producer warp:   coalesced 16-byte cp.async of a unit's latent rows (one
-//                    contiguous block in HBM) into a ring of shared-memory stages,
-//                    rows padded to an odd number of 16-byte chunks so that
-//                    row-per-thread reads are conflict-free; each lane's copies
-//                    arrive on the stage's mbarrier when they complete;
-//   converter warpgroup: thread = token row; reads its staged row, converts to
-//                    fp16 (int8 codes are exact in fp16) and writes it into one
-//                    of 4 A buffers in TMEM with tcgen05.st — the A operand never
+// one (tile, query head) pair.  Roles, handing off through mbarriers (every wait
+// bounded):
+//   producer warp:   one 1-D bulk copy per unit (its rows are one contiguous
+//                    block in HBM) into a ring of tile slots in shared memory;
+//   converter warpgroups (2, alternate units): thread = token row; converts its
+//                    staged row to fp16 (int8 codes are exact in fp16) into
+//                    registers, releases the stage, waits for its own A buffer in
+//                    TMEM and writes it with wide tcgen05.st — the A operand never
 //                    touches shared memory;
-//   MMA thread:      per job r/16 tcgen05.mma (A from TMEM, B = W_g from shared
-//                    memory, M=128, N=128, K=16) into one of 2 TMEM accumulators;
-//   drain warpgroups: both take every job; warpgroup h owns the frequencies
-//                    [32h, 32h + 32): one tcgen05.ld of its token's 64 accumulator
-//                    columns (the accumulator is released right after) and the
-//                    RoPE-weighted partial sum (packed fp32x2 FMA) into a ring of
-//                    partials in shared memory;
-//   finaliser warps 2, 3 (alternate jobs): sum of the two partials, scale, mask,
-//                    logits to global, and a running maximum per head — the split
-//                    maximum the V kernel's softmax starts from (the V kernel forms
-//                    the exponentials and their sums itself).
-// TMEM columns: [0, 256) the two accumulators, [256, 512) four A buffers of 64
+//   MMA issuers (warps 1 and 2 for one-job units, else warp 1): per job r/16
+//                    tcgen05.mma (A from TMEM, B = W_g from shared memory, M=128,
+//                    N=128, K=16) into accumulator j mod 3;
+//   drain warpgroups (2, alternate tiles): thread = token row; eight 16-column
+//                    tcgen05.ld of the accumulator (released right after), the
+//                    RoPE-weighted sum over all 64 frequencies (packed fp32x2 FMA),
+//                    scale, mask, the logit to global and a running maximum per
+//                    head — the split maximum the V kernel's softmax starts from
+//                    (the V kernel forms the exponentials and their sums itself).
+// TMEM columns: [0, 384) three accumulators, [384, 512) two A buffers of 64
 // columns (r <= 128 fp16 values per row).
 //
 // RoPE angles: each drain thread owns one token row; it starts from cos/sin of
-// l*w_i for its first token and advances by the exact rotation through
-// 128*w_i when its tile changes (fp32, 4 FMA per frequency per tile,
-// shared by the heads of the tile).  The angles are the exact l*w_i; the
-// reference's fp32 product fl(l*w_i) differs from them by at most half an ulp of
-// the angle.
+// l*w_i for the first token of its first tile and advances by the exact rotation
+// through 256*w_i to its next tile (fp32, packed FMAs, shared by the G heads of
+// the tile).  The angles are the exact l*w_i; the reference's fp32 product
+// fl(l*w_i) differs from them by at most half an ulp of the angle.
 #pragma once
 #include "common.cuh"
 #include "sm100.cuh"
@@ -426,7 +422,6 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   int* s_run0 = reinterpret_cast<int*>(smem + 576);           // [4] first head of run n
   int* s_runlen = reinterpret_cast<int*>(smem + 592);         // [4] heads in run n
   float* s_red = reinterpret_cast<float*>(smem + 704);        // [64]
-  float2* s_rot = reinterpret_cast<float2*>(smem + 1024);     // [64] rotation by 128 positions
   float4* s_rot4 = reinterpret_cast<float4*>(smem + 4096);    // [32] rotation by 256 positions per frequency pair (cos.xy, sin.xy)
   float* s_qall = reinterpret_cast<float*>(smem + 1536);      // [4][128]
   uint8_t* Bsm = smem + kKHeader;
@@ -593,11 +588,6 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       } else {
         for (int e = bt; e < G * 128; e += 512)
           s_qall[e] = load_as_f32(p.q, p.q_dtype, ((int64_t)b * Hq + grp * G) * 128 + e);
-      }
-      if (bt < 64) {
-        float c, sn;
-        exact_sincos(128, p.inv_freq[bt], c, sn);
-        s_rot[bt] = make_float2(c, sn);
       }
       named_bar_sync(2, 512);
       if (bt >= 64 && bt < 96) {                       // rotation of the pair (2i, 2i + 1) by 256 positions: cos, sin

@@ -154,7 +154,6 @@ namespace starkv {
 // reference's projection output) and quantises exactly as the append kernels do;
 // k_out / v_out optionally receive the rounded latents.
 constexpr int kPaWarps = 8;
-constexpr int kPaSeq = 8;          // sequences per CTA (grid.y = batch passes)
 template <typename LT>
 __host__ __device__ constexpr int kPaSeqOf() { return 8; }
 
