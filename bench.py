@@ -203,15 +203,29 @@ def main():
     dev = torch.device("cuda", local)
     from starkv import dist as sd
     from starkv import ops
-    from starkv.harness import device_layer
+    from starkv.harness import device_layer, shard_layer
 
     if world > 1:
         sd.init("nccl", timeout_s=300, device_id=dev)
         sd.check_partition(spec, device=dev)
-    sub = sd.shard_spec(spec, rank, world) if world > 1 else spec
-    st, _, _ = device_layer(sub, dev, seed=1 + rank)
+    full = None
+    if world > 1:
+        # every rank builds the same seeded full layer and cuts its heads out of it,
+        # so the gathered sharded output can be checked against the full step
+        full, k_u_heads, v_u_full = device_layer(spec, dev, seed=1)
+        sub = sd.shard_spec(spec, rank, world)
+        st = shard_layer(full, k_u_heads, v_u_full, spec, sub, rank, world)
+        del k_u_heads, v_u_full
+        full.k_lat = full.v_lat = None
+        if rank != 0:
+            full = None
+        torch.cuda.empty_cache()
+    else:
+        sub = spec
+        st, _, _ = device_layer(sub, dev, seed=1)
     layer = st.layer
     layer.num_splits = args.splits
+    layout_full = ops.layout_from_spec(spec) if world > 1 else None
     L = sub.context
     B, hq = sub.batch, sub.num_q_heads
     out = torch.empty(B, hq, 128, dtype=st.q.dtype, device=dev)
@@ -296,6 +310,26 @@ def main():
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "api": "starkv.layer.DecodeLayer.step (C ABI starkv_append + starkv_decode_attention)"}
 
+    # ---- N > 1: the gathered sharded output against the full layer's step on rank 0
+    check = None
+    if world > 1:
+        ns_full = ops.auto_splits(layout_full, spec.tokens)
+        layer.num_splits = ns_full                 # the full step's K splits: same tile boundaries
+        layer.cache.length = L
+        layer.step(st.q, st.k_new, st.v_new, out=out)
+        got = sd.gather_heads(out, buffer=gathered).clone()
+        if rank == 0:
+            full.layer.num_splits = ns_full
+            full.layer.cache.length = L
+            ref = full.layer.step(full.q, full.k_new, full.v_new)
+            torch.cuda.synchronize()
+            if torch.equal(got, ref):
+                check = "bit-exact"
+            else:
+                d = (got.float() - ref.float()).abs().max().item()
+                check = f"MISMATCH max_abs={d:.3e}"
+        dist.barrier()
+
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -329,6 +363,8 @@ def main():
         "e2e": e2e,
         "clocks": clk.summary(),
     }
+    if check is not None:
+        line["check"] = check
     if world == 1 and not args.no_cpu:
         t = cpu_sample(spec)
         line["cpu_baseline"] = {"value": 1.0 / t, "unit": UNIT, "cores": cpu_cores(), "kind": "port",

@@ -216,6 +216,12 @@ int starkv_decode_attention_static(const starkv_layout* lay, const starkv_decode
 /* Size in bytes of the static scratch used by starkv_decode_attention_static. */
 size_t starkv_static_scratch_bytes(void);
 
+/* starkv_read_device_error for the static scratch of starkv_decode_attention_static
+ * (whose callers never see its address): reads and clears the device error word
+ * that a timed-out device wait leaves there (synchronises the stream).  No
+ * counterpart in the reference. */
+int starkv_static_read_device_error(int* out_code, starkv_stream_t stream);
+
 /*
  * Diagnostics: when `buffer` is non-NULL, later K-path launches record a
  * per-job clock64 timeline (10 int64 fields per job, `jobs` jobs) of the CTAs

@@ -744,6 +744,14 @@ extern "C" {
 
 size_t starkv_static_scratch_bytes(void) { return kStaticScratchBytes; }
 
+int starkv_static_read_device_error(int* out_code, starkv_stream_t stream) {
+  if (!out_code) return set_error(STARKV_ERR_INVALID, "null out_code");
+  int rc = STARKV_OK;
+  uint8_t* scratch = static_scratch_ptr(&rc);
+  if (rc) return rc;
+  return starkv_read_device_error(scratch, out_code, stream);
+}
+
 int starkv_decode_attention_static(const starkv_layout* lay, const starkv_decode_args* args,
                                    starkv_stream_t stream) {
   int rc = validate(lay);

@@ -70,6 +70,7 @@ SIGNATURES = [
     ("starkv_debug_trace", C.c_int, [C.c_void_p, C.c_int32]),
     ("starkv_decode_attention_static", C.c_int, [C.POINTER(Layout), C.POINTER(DecodeArgs), C.c_void_p]),
     ("starkv_static_scratch_bytes", C.c_size_t, []),
+    ("starkv_static_read_device_error", C.c_int, [C.POINTER(C.c_int), C.c_void_p]),
     ("starkv_read_device_error", C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.c_void_p]),
     ("starkv_last_error", C.c_char_p, []),
 ]

@@ -24,14 +24,27 @@ import torch
 import torch.distributed as dist
 
 
-def shard_spec(spec, rank: int, world: int):
-    """LayerSpec of the heads rank `rank` owns: a contiguous range of whole V blocks."""
+def shard_range(spec, rank: int, world: int):
+    """(first V block, end V block, first KV head, end KV head) of ``rank``: a
+    contiguous range of whole V blocks.  Every rank must get the same number of
+    query heads (the per-head outputs are gathered with one equal-sized
+    all-gather), so V blocks covering different KV-head counts per rank are
+    rejected."""
     nb = spec.num_v_blocks
     if world <= 0 or nb % world:
         raise ValueError(f"{nb} V blocks do not split evenly over {world} ranks")
     per = nb // world
+    counts = {sum(spec.v_block_kv[r * per:(r + 1) * per]) for r in range(world)}
+    if len(counts) != 1:
+        raise ValueError(f"V blocks give the {world} ranks different KV-head counts {sorted(counts)}: "
+                         "the equal-sized head all-gather needs equal shards")
     b0, b1 = rank * per, (rank + 1) * per
-    kv0, kv1 = sum(spec.v_block_kv[:b0]), sum(spec.v_block_kv[:b1])
+    return b0, b1, sum(spec.v_block_kv[:b0]), sum(spec.v_block_kv[:b1])
+
+
+def shard_spec(spec, rank: int, world: int):
+    """LayerSpec of the heads rank `rank` owns: a contiguous range of whole V blocks."""
+    b0, b1, kv0, kv1 = shard_range(spec, rank, world)
     qpk = spec.num_q_heads // spec.num_kv_heads
     sub = copy.deepcopy(spec)
     sub.k_ranks = list(spec.k_ranks[kv0:kv1])

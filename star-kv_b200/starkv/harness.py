@@ -86,3 +86,25 @@ def device_layer(spec, device="cuda", seed: int = 0):
     layer.prefill(k_lat[:, :L].contiguous(), v_lat[:, :L].contiguous())
     step = StepInputs(layer, q, k_lat[:, L:].contiguous(), v_lat[:, L:].contiguous(), None, k_lat, v_lat)
     return step, k_u_heads, v_u
+
+
+def shard_layer(step: StepInputs, k_u_heads: List[torch.Tensor], v_u: torch.Tensor, spec, sub, rank: int,
+                world: int) -> StepInputs:
+    """The decode state of the heads ``rank`` owns, cut out of a full layer built
+    by ``device_layer`` (same latents, up-projections and query as the full
+    layer, so the gathered sharded outputs can be compared with the full step)."""
+    from .dist import shard_range
+    b0, b1, kv0, kv1 = shard_range(spec, rank, world)
+    qpk = spec.num_q_heads // spec.num_kv_heads
+    kcol = np.concatenate([[0], np.cumsum(spec.k_ranks)]).astype(int)
+    vcol = np.concatenate([[0], np.cumsum(spec.v_ranks)]).astype(int)
+    k_lat = step.k_lat[:, :, kcol[kv0]:kcol[kv1]].contiguous()
+    v_lat = step.v_lat[:, :, vcol[b0]:vcol[b1]].contiguous()
+    dev = step.q.device
+    layout = ops.layout_from_spec(sub)
+    layer = DecodeLayer(layout, pack_k_u(k_u_heads[kv0:kv1]),
+                        v_u[kv0 * 128:kv1 * 128, vcol[b0]:vcol[b1]].contiguous(), sub.theta, device=dev)
+    L = spec.context
+    layer.prefill(k_lat[:, :L].contiguous(), v_lat[:, :L].contiguous())
+    q = step.q[:, kv0 * qpk:kv1 * qpk].contiguous()
+    return StepInputs(layer, q, k_lat[:, L:].contiguous(), v_lat[:, L:].contiguous(), None)

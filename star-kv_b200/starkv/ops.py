@@ -194,6 +194,11 @@ def workspace(nbytes: int, device) -> torch.Tensor:
     return ws
 
 
+def auto_splits(layout: Layout, num_tokens: int) -> int:
+    """Sequence splits the decode step picks for this layout and token count."""
+    return int(load().starkv_auto_splits(C.byref(layout), int(num_tokens)))
+
+
 def workspace_size(layout: Layout, num_tokens: int, num_splits: int = 0) -> int:
     n = C.c_size_t(0)
     check(load().starkv_decode_workspace_size(C.byref(layout), num_tokens, num_splits, C.byref(n)),
@@ -266,6 +271,14 @@ def decode_attention_static(layout: Layout, cache: LatentCache, q: torch.Tensor,
     check(load().starkv_decode_attention_static(C.byref(layout), C.byref(a), _stream()),
           "starkv_decode_attention_static")
     return out
+
+
+def static_read_device_error() -> int:
+    """Read and clear the device error word of the static scratch used by
+    ``decode_attention_static`` (synchronises)."""
+    code = C.c_int(0)
+    check(load().starkv_static_read_device_error(C.byref(code), _stream()), "starkv_static_read_device_error")
+    return int(code.value)
 
 
 def k_logits(layout: Layout, cache: LatentCache, q: torch.Tensor, k_u: torch.Tensor, inv_freq: torch.Tensor,

@@ -134,6 +134,15 @@ def test_shard_spec_partitions_heads():
         sd.shard_spec(spec, 0, 3)
 
 
+def test_uneven_v_blocks_are_rejected():
+    """V blocks of different KV-head counts would give ranks different head
+    counts; the equal-sized all-gather cannot collect those, so sharding refuses."""
+    spec = make_spec("c1", num_q_heads=12, v_block_kv=[4, 8], v_ranks=[64, 128])
+    with pytest.raises(ValueError, match="different KV-head counts"):
+        sd.shard_spec(spec, 0, 2)
+    assert sd.shard_spec(spec, 0, 1).num_q_heads == 12
+
+
 def test_sharded_decode_gathers_to_the_full_layer():
     res = _run(_sharded_worker)
     oks = [r for r in res if r[0] == "ok"]
