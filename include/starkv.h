@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define STARKV_ABI_VERSION 1
+#define STARKV_ABI_VERSION 2
 #define STARKV_MAX_KV_HEADS 64
 #define STARKV_MAX_V_BLOCKS 32
 #define STARKV_HEAD_DIM 128
@@ -58,11 +58,19 @@ typedef enum starkv_dtype {
 /*
  * Layout of one layer's latent cache.
  *
- * K (per KV head h, rank r_h = k_rank[h], multiple of 16, <= 128): element
- *   (b, slot, c) lives at  k_offset[h] + b * k_batch_stride[h] + slot * r_h + c
- *   in units of the cache element (int8 code when quantised, latent dtype
- *   otherwise).  The reference's (B, Hkv, L, r) tensor is k_offset[h] = h*L*r,
- *   k_batch_stride = Hkv*L*r.
+ * K (per KV head h, rank r_h = k_rank[h], multiple of 16, <= 128), in units
+ *   of the cache element (int8 code when quantised, latent dtype otherwise;
+ *   e bytes, n = 16 / e elements per 16-byte chunk):
+ *   row-major (k_tiled = 0): element (b, slot, c) lives at
+ *     k_offset[h] + b * k_batch_stride[h] + slot * r_h + c;
+ *     the reference's (B, Hkv, L, r) tensor is k_offset[h] = h*L*r,
+ *     k_batch_stride = Hkv*L*r;
+ *   tiled (k_tiled = 1, capacity a multiple of 128): tiles of 128 slots, each
+ *     the r_h / n column chunks of its 128 rows, a chunk 128 x 16 bytes:
+ *     k_offset[h] + b * k_batch_stride[h] + (slot / 128) * 128 * r_h
+ *       + (c / n) * 128 * n + (slot % 128) * n + c % n.
+ *     A 16-byte piece of 128 consecutive rows is one contiguous 2 KiB run: the
+ *     K kernel reads its staged tiles without shared-memory bank conflicts.
  * K scales (quantised): fp16, (B, sum r_h): scale(b, h, c) at b*k_rank_total + k_col[h] + c.
  * V (blocks j of v_num_kv[j] consecutive KV heads starting at v_first_kv[j],
  *   rank r_j = v_rank[j], multiple of 32): the latents of all blocks of one
@@ -84,7 +92,7 @@ typedef struct starkv_layout {
   int32_t latent_dtype;    /* starkv_dtype of latents fed to the quantiser / stored unquantised */
   int32_t k_rank_total;    /* sum k_rank */
   int32_t v_rank_total;    /* sum v_rank = R */
-  int32_t reserved;
+  int32_t k_tiled;         /* 1: K tiles of 128 slots stored as 16-byte column chunks (see above) */
   int32_t k_rank[STARKV_MAX_KV_HEADS];
   int32_t k_col[STARKV_MAX_KV_HEADS];          /* prefix sums of k_rank */
   int64_t k_offset[STARKV_MAX_KV_HEADS];
@@ -156,7 +164,8 @@ typedef struct starkv_decode_args {
   const void* v_params;
   void* out;                /* (B, Hq, 128) out_dtype */
   int32_t out_dtype;
-  int32_t num_splits;       /* sequence splits per (sequence, head group); 0 = automatic */
+  int32_t num_splits;       /* sequence splits of the V pass per sequence; 0 = automatic (the K pass
+                               balances its own work over the SMs) */
   void* workspace;          /* scratch, 256-byte aligned */
   size_t workspace_bytes;
   void* const* events;      /* optional: 4 cudaEvent_t recorded on the stream before the K kernel, after
@@ -167,7 +176,7 @@ typedef struct starkv_decode_args {
 int starkv_decode_workspace_size(const starkv_layout* lay, int32_t num_tokens, int32_t num_splits,
                                  size_t* bytes);
 
-/* Number of sequence splits the automatic choice (num_splits = 0) uses. */
+/* Number of V-pass sequence splits the automatic choice (num_splits = 0) uses. */
 int32_t starkv_auto_splits(const starkv_layout* lay, int32_t num_tokens);
 
 /*
@@ -183,7 +192,8 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
 /*
  * Logits only (abx_rope_batched.abx): logits[b, qh, l] = q[b, qh] . RoPE_l(X_k[b, kv(qh), l] @ U^T)
  * for l < num_tokens, unscaled, fp32, (B, Hq, num_tokens) contiguous.  The
- * args' mask / v_* / out / workspace fields are ignored.
+ * args' workspace (starkv_decode_workspace_size bytes) holds the per-head W
+ * images; mask / v_* / out are ignored.
  */
 int starkv_k_logits(const starkv_layout* lay, const starkv_decode_args* args, float* logits,
                     starkv_stream_t stream);
@@ -223,13 +233,26 @@ size_t starkv_static_scratch_bytes(void);
 int starkv_static_read_device_error(int* out_code, starkv_stream_t stream);
 
 /*
- * Diagnostics: when `buffer` is non-NULL, later K-path launches record a
- * per-job clock64 timeline (10 int64 fields per job, `jobs` jobs) of the CTAs
- * (split 0, head group 0, sequence 0 and 1) into it: converter begin / codes
- * landed / A buffer free / converted / A published, MMA issue, drain wait /
- * accumulator ready / drain done.  NULL turns it off.  Not for production use.
+ * The reference's split quantiser (quant_utils.quantize_r_split_int8_int4_packed,
+ * called at LlamaLoRaAttention_headwise_quant.py:107-117, absent from the reference
+ * tree): x (rows, r) of dtype -> per row, ranks [0, split_r) as int8 up_q
+ * (rows, split_r) with fp16 scale s_up (rows) = absmax / 127, ranks [split_r, r)
+ * as signed int4 lo_q (rows, ceil((r - split_r) / 2)) packed as nibble q + 8
+ * (even rank low) with fp16 scale s_lo (rows) = absmax / 7.  Symmetric,
+ * round-half-even, IEEE fp32; a zero row gets scale 1.
  */
-int starkv_debug_trace(void* buffer, int32_t jobs);
+int starkv_quantize_split(const void* x, int32_t dtype, int64_t rows, int32_t r, int32_t split_r, void* up_q,
+                          void* s_up, void* lo_q, void* s_lo, starkv_stream_t stream);
+
+/*
+ * Test hooks for the device-side failure path (no counterpart in the
+ * reference): wait_limit_ns (> 0; 0 restores the default 2 s) bounds every
+ * mbarrier wait of the K kernel; skip_copy_unit >= 0 makes the K kernel's
+ * first CTA never issue that unit's staging copy, so that its consumers' waits
+ * run out, record an error code in the workspace's first word and return.
+ * (0, -1) restores normal operation.  Not for production use.
+ */
+int starkv_set_test_hooks(int64_t wait_limit_ns, int32_t skip_copy_unit);
 
 /* Reads and clears the device error word at the start of a decode workspace
  * (synchronises the stream); *out_code = 0 means no device-side error. */

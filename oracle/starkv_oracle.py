@@ -137,6 +137,44 @@ def dequant_v(packed: np.ndarray, scale: np.ndarray, zero: np.ndarray) -> np.nda
 
 
 # ---------------------------------------------------------------------------
+# Split quantiser of the reference's quantised module (quant_utils interface,
+# call sites LlamaLoRaAttention_headwise_quant.py:107-117, 137-140, 164-165;
+# dequantisation (nib - 8) * scale as bx_quant.py:75-86).  Specification (the
+# module is absent from the reference): per row, ranks [0, split_r) int8 with
+# s = fp16(absmax / 127), the rest signed int4 with s = fp16(absmax / 7),
+# q = clamp(rint(x / s)), nibble q + 8, even rank in the low nibble; zero rows
+# get s = 1.
+# ---------------------------------------------------------------------------
+
+def quantize_split(x: np.ndarray, split_r: int):
+    x = x.astype(F32)
+    r = x.shape[-1]
+    r4 = r - split_r
+
+    def scale(part, qmax):
+        s = (np.max(np.abs(part), axis=-1, keepdims=True).astype(F32) / F32(qmax)).astype(F32).astype(np.float16)
+        s[s == 0] = np.float16(1.0)
+        return s
+
+    up, lo = x[..., :split_r], x[..., split_r:]
+    s_up = scale(up, 127.0) if split_r else np.ones(x.shape[:-1] + (1,), np.float16)
+    s_lo = scale(lo, 7.0) if r4 else np.ones(x.shape[:-1] + (1,), np.float16)
+    up_q = np.clip(np.rint((up / s_up.astype(F32)).astype(F32)), -127, 127).astype(np.int8)
+    q = np.clip(np.rint((lo / s_lo.astype(F32)).astype(F32)), -8, 7).astype(np.int16) + 8
+    if r4 % 2:
+        q = np.concatenate([q, np.zeros(q.shape[:-1] + (1,), q.dtype)], axis=-1)
+    lo_q = (q[..., 0::2] | (q[..., 1::2] << 4)).astype(np.uint8)
+    return up_q, s_up, lo_q, s_lo, r4
+
+
+def unpack_int4_signed(q: np.ndarray, r: int) -> np.ndarray:
+    out = np.empty(q.shape[:-1] + (2 * q.shape[-1],), dtype=np.int8)
+    out[..., 0::2] = (q & 0x0F).astype(np.int8) - 8
+    out[..., 1::2] = ((q >> 4) & 0x0F).astype(np.int8) - 8
+    return out[..., :r]
+
+
+# ---------------------------------------------------------------------------
 # Decode attention (headwise.py:98-146 reorder branch; model.py:450-487 GQA)
 # ---------------------------------------------------------------------------
 

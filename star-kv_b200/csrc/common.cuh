@@ -58,11 +58,34 @@ __device__ __forceinline__ void store_from_f32(void* p, int dtype, int64_t i, fl
 
 __host__ __device__ __forceinline__ int dtype_bytes(int dtype) { return dtype == STARKV_F32 ? 4 : 2; }
 
+// Element index of K latent / code (b, slot, c) of KV head kv (element size eb
+// bytes).  Row-major: rows of r elements.  Tiled (lay.k_tiled): tiles of 128
+// slots, each stored as r*eb/16 column chunks of 128 rows x 16 bytes, so that
+// one 16-byte chunk of consecutive rows is contiguous.
+__host__ __device__ __forceinline__ int64_t k_elem(const starkv_layout& l, int kv, int b, int64_t slot, int c,
+                                                   int eb) {
+  const int64_t base = l.k_offset[kv] + (int64_t)b * l.k_batch_stride[kv];
+  const int r = l.k_rank[kv];
+  if (!l.k_tiled) return base + slot * r + c;
+  const int per = 16 / eb;
+  return base + (slot >> 7) * 128 * r + (int64_t)(c / per) * 128 * per + (slot & 127) * per + (c % per);
+}
+
 // Combine two (max, sum-of-exp2) softmax partials in log2 domain.
 __device__ __forceinline__ void softmax_merge(float& m, float& l, float m2, float l2) {
   const float mn = fmaxf(m, m2);
   l = l * exp2f(m - mn) + l2 * exp2f(m2 - mn);
   m = mn;
+}
+
+// Atomic maximum of a float in global memory (sign-split integer atomics on the
+// IEEE bit pattern: non-negative floats order like signed ints, negative ones
+// like reversed unsigned ints).
+__device__ __forceinline__ void atomic_max_float(float* addr, float v) {
+  if (v >= 0.f)
+    atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
+  else
+    atomicMin(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
 }
 
 // Finite "minus infinity" so that (m - m) never produces NaN.

@@ -45,12 +45,11 @@ __global__ void __launch_bounds__(256) k_prefill_quant_kernel(const starkv_layou
     sc[c] = __half2float(h);
   }
   __syncthreads();
-  int8_t* dst = k_cache + lay.k_offset[kv] + (int64_t)b * lay.k_batch_stride[kv];
   for (int64_t e = threadIdx.x; e < (int64_t)T * r; e += blockDim.x) {
     const int t = (int)(e / r), c = (int)(e % r);
     float q = rintf(__fdiv_rn(to_f32(src[(int64_t)t * K + c]), sc[c]));
     q = fminf(fmaxf(q, -127.f), 127.f);
-    dst[(int64_t)t * r + c] = (int8_t)(int)q;
+    k_cache[k_elem(lay, kv, b, t, c, 1)] = (int8_t)(int)q;
   }
 }
 
@@ -68,11 +67,10 @@ __global__ void __launch_bounds__(256) k_append_quant_kernel(const starkv_layout
     int kv = 0;
     while (kv + 1 < lay.num_kv_heads && lay.k_col[kv + 1] <= ch) ++kv;
     const int c = ch - lay.k_col[kv];
-    const int r = lay.k_rank[kv];
     const float s = __half2float(k_scales[(int64_t)b * K + ch]);
     float q = rintf(__fdiv_rn(to_f32(k_lat[e]), s));
     q = fminf(fmaxf(q, -127.f), 127.f);
-    k_cache[lay.k_offset[kv] + (int64_t)b * lay.k_batch_stride[kv] + (int64_t)(start + t) * r + c] = (int8_t)(int)q;
+    k_cache[k_elem(lay, kv, b, start + t, c, 1)] = (int8_t)(int)q;
   }
 }
 
@@ -126,8 +124,8 @@ __global__ void __launch_bounds__(256) copy_append_kernel(const starkv_layout la
       const int t = (int)(bt % T), b = (int)(bt / T);
       int kv = 0;
       while (kv + 1 < lay.num_kv_heads && lay.k_col[kv + 1] <= ch) ++kv;
-      const int c = ch - lay.k_col[kv], r = lay.k_rank[kv];
-      k_cache[lay.k_offset[kv] + (int64_t)b * lay.k_batch_stride[kv] + (int64_t)(start + t) * r + c] = k_lat[e];
+      const int c = ch - lay.k_col[kv];
+      k_cache[k_elem(lay, kv, b, start + t, c, (int)sizeof(LT))] = k_lat[e];
     } else {
       const int64_t f = e - nk;
       const int ch = (int)(f % R);
@@ -250,8 +248,8 @@ __global__ void __launch_bounds__(kPaWarps * 32) project_append_kernel(
           const int ch = c0 + lane;
           int kv = 0;
           while (kv + 1 < lay.num_kv_heads && lay.k_col[kv + 1] <= ch) ++kv;
-          const int c = ch - lay.k_col[kv], r = lay.k_rank[kv];
-          const int64_t dst = lay.k_offset[kv] + (int64_t)b * lay.k_batch_stride[kv] + (int64_t)slot * r + c;
+          const int c = ch - lay.k_col[kv];
+          const int64_t dst = k_elem(lay, kv, b, slot, c, QUANT ? 1 : (int)sizeof(LT));
           if (k_out) k_out[(int64_t)b * K + ch] = lat;
           if constexpr (QUANT) {
             const float sc = __half2float(k_scales[(int64_t)b * K + ch]);
@@ -286,6 +284,57 @@ __global__ void __launch_bounds__(kPaWarps * 32) project_append_kernel(
           reinterpret_cast<LT*>(v_cache)[rowi * R + c0 + lane] = lat;
         }
       }
+    }
+  }
+}
+
+// ---- split format of the reference's quantiser interface
+// (quantize_r_split_int8_int4_packed, called at LlamaLoRaAttention_headwise_quant.py:107-117):
+// per row, the first split_r values as int8 with one symmetric fp16 scale
+// (absmax / 127), the rest as signed int4 with one symmetric fp16 scale
+// (absmax / 7), stored as nibble q + 8, even rank in the low nibble.  One warp per row.
+template <typename LT>
+__global__ void __launch_bounds__(256) split_quant_kernel(const LT* __restrict__ x, int64_t rows, int r, int split_r,
+                                                          int8_t* __restrict__ up, __half* __restrict__ s_up,
+                                                          uint8_t* __restrict__ lo, __half* __restrict__ s_lo) {
+  const int lane = threadIdx.x & 31;
+  const int r4 = r - split_r;
+  for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < rows;
+       w += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const LT* xr = x + w * r;
+    float au = 0.f, al = 0.f;
+    for (int c = lane; c < r; c += 32) {
+      const float v = fabsf(to_f32(xr[c]));
+      if (c < split_r) au = fmaxf(au, v); else al = fmaxf(al, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      au = fmaxf(au, __shfl_xor_sync(0xffffffffu, au, o));
+      al = fmaxf(al, __shfl_xor_sync(0xffffffffu, al, o));
+    }
+    __half hu = __float2half_rn(__fdiv_rn(au, 127.0f)), hl = __float2half_rn(__fdiv_rn(al, 7.0f));
+    if (__half2float(hu) == 0.0f) hu = __float2half_rn(1.0f);
+    if (__half2float(hl) == 0.0f) hl = __float2half_rn(1.0f);
+    if (lane == 0) {
+      if (split_r > 0) s_up[w] = hu;
+      if (r4 > 0) s_lo[w] = hl;
+    }
+    const float su = __half2float(hu), sl = __half2float(hl);
+    for (int c = lane; c < split_r; c += 32) {
+      const float q = fminf(fmaxf(rintf(__fdiv_rn(to_f32(xr[c]), su)), -127.f), 127.f);
+      up[w * split_r + c] = (int8_t)(int)q;
+    }
+    for (int c2 = lane; c2 < (r4 + 1) / 2; c2 += 32) {
+      uint32_t byte = 0;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int c = 2 * c2 + k;
+        if (c < r4) {
+          const float q = fminf(fmaxf(rintf(__fdiv_rn(to_f32(xr[split_r + c]), sl)), -8.f), 7.f);
+          byte |= ((uint32_t)((int)q + 8) & 0xFu) << (4 * k);
+        }
+      }
+      lo[w * ((r4 + 1) / 2) + c2] = (uint8_t)byte;
     }
   }
 }

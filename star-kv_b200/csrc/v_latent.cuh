@@ -446,11 +446,8 @@ struct V2Params {
   int* err;
   int T, nsplit, nsplit_k, tps, rv_max;
   int nstages, stage_bytes, b_bytes;
-  long long* trace;      // optional per-tile clock64 timeline of CTA (0, 0); null = off
-  int trace_tiles;
 };
 
-enum V2Trace { kV2TrIssue = 0, kV2TrStage, kV2TrDequant, kV2TrProbs, kV2TrMmaB, kV2TrMmaDone, kV2TrFields = 8 };
 
 __host__ __device__ inline int v2_stage_bytes(int R) {
   return ((kV2Tile * (R / 2) + kV2Tile * (R / 8) + 32) + 127) & ~127;
@@ -604,11 +601,6 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
     record_error(p.err, code);
     *s_abort = 1;
   };
-  long long* trace = (p.trace && split == 0 && b == 0) ? p.trace : nullptr;
-  auto stamp = [&](int t, int f) {
-    if (trace && t < p.trace_tiles) trace[(int64_t)t * kV2TrFields + f] = clock64();
-  };
-  long long* mtrace = trace ? trace + (int64_t)p.trace_tiles * kV2TrFields : nullptr;   // per M unit: 4 fields
 
   if (warp == 0) {
     // ============================================================ producer
@@ -618,7 +610,6 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         if (*s_abort) break;
         const int s = t % NS;
         if (!mbar_wait(st_empty + s, (uint32_t)(((t / NS) & 1) ^ 1))) { fail(kDevWaitCopy); break; }
-        stamp(t, kV2TrIssue);
         const int t0 = t_begin + t * kV2Tile;
         const int nrows = min(kV2Tile, t_end - t0);
         const int64_t row0 = (int64_t)b * lay.capacity + t0;
@@ -656,13 +647,11 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         if (*s_abort) break;
         const int tb = t & 1;
         if (!mbar_wait(b_full + tb, (uint32_t)((t >> 1) & 1))) { ok = false; break; }
-        stamp(t, kV2TrMmaB);
         const uint32_t bt = smem_u32(Bsm + tb * p.b_bytes);
         for (int m = 0; m < MU; ++m, ++mc) {
           const int k = mc % kV2Abufs;
           if (!mbar_wait(a_full + k, (uint32_t)((mc / kV2Abufs) & 1))) { ok = false; break; }
           tc_fence_after();
-          if (mtrace && mc < p.trace_tiles) mtrace[mc * 4 + 2] = clock64();
           const uint64_t ad = smem_desc(smem_u32(Asm + k * kV2ABytes), 128, 1024);
           const uint64_t bd = smem_desc(bt, 128, 1024);
           const uint32_t d = tmem + (uint32_t)(m * NP);
@@ -670,10 +659,8 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
           for (int ks = 0; ks < kV2Tile / 16; ++ks)
             mma_f16_ss(d, ad + (uint64_t)(ks * 16), bd + (uint64_t)(ks * 16), IDESC, (t > 0 || ks > 0) ? 1u : 0u);
           mma_commit(a_empty + k);
-          if (mtrace && mc < p.trace_tiles) mtrace[mc * 4 + 3] = clock64();
         }
         mma_commit(b_empty + tb);
-        stamp(t, kV2TrMmaDone);
       }
       if (!ok) fail(kDevWaitMma);
       mma_commit(fin_bar);
@@ -740,7 +727,6 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(b_full + tb);
-      if (tid == 64) stamp(t, kV2TrProbs);
     }
     if (!ok) fail(kDevWaitMma);
     // sum over the 4 lanes of a head (same lane & 7), then over the two warps
@@ -766,7 +752,6 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       if (*s_abort) break;
       const int s = t % NS;
       if (!mbar_wait(st_full + s, (uint32_t)((t / NS) & 1))) { ok = false; break; }
-      if (tid == 128) stamp(t, kV2TrStage);
       const uint8_t* codes = Ssm + (size_t)s * p.stage_bytes;
       const uint8_t* pars = codes + kV2Tile * code_row;
       const int t0 = t_begin + t * kV2Tile;
@@ -780,7 +765,6 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         const int k = mc % kV2Abufs;
         if (k != pair) continue;
         if (!mbar_wait(a_empty + k, (uint32_t)(((mc / kV2Abufs) & 1) ^ 1))) { ok = false; break; }
-        if (mtrace && mc < p.trace_tiles && pl == 0) mtrace[mc * 4 + 0] = clock64();
         const int c0 = m * 128;                              // first global channel of the M unit
         const int nch = min(128, R - c0);
         const int gc = nch >> 5;                             // 32-channel groups in the M tile
@@ -794,11 +778,9 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(a_full + k);
-        if (mtrace && mc < p.trace_tiles && pl == 0) mtrace[mc * 4 + 1] = clock64();
       }
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(st_empty + s);
-      if (tid == 128) stamp(t, kV2TrDequant);
     }
     if (!ok) fail(kDevWaitMma);
     // ---- epilogue: accumulators -> split partials (warp quarter = TMEM lanes)

@@ -11,7 +11,7 @@ import os
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libstarkv.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 MAX_KV_HEADS = 64
 MAX_V_BLOCKS = 32
 
@@ -27,7 +27,7 @@ class Layout(C.Structure):
         ("abi_version", C.c_int32), ("batch", C.c_int32), ("num_q_heads", C.c_int32),
         ("num_kv_heads", C.c_int32), ("head_dim", C.c_int32), ("num_v_blocks", C.c_int32),
         ("capacity", C.c_int32), ("quantized", C.c_int32), ("latent_dtype", C.c_int32),
-        ("k_rank_total", C.c_int32), ("v_rank_total", C.c_int32), ("reserved", C.c_int32),
+        ("k_rank_total", C.c_int32), ("v_rank_total", C.c_int32), ("k_tiled", C.c_int32),
         ("k_rank", C.c_int32 * MAX_KV_HEADS), ("k_col", C.c_int32 * MAX_KV_HEADS),
         ("k_offset", C.c_int64 * MAX_KV_HEADS), ("k_batch_stride", C.c_int64 * MAX_KV_HEADS),
         ("v_rank", C.c_int32 * MAX_V_BLOCKS), ("v_col", C.c_int32 * MAX_V_BLOCKS),
@@ -67,7 +67,9 @@ SIGNATURES = [
     ("starkv_k_logits", C.c_int, [C.POINTER(Layout), C.POINTER(DecodeArgs), C.c_void_p, C.c_void_p]),
     ("starkv_v_latent", C.c_int, [C.POINTER(Layout), C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_void_p]),
-    ("starkv_debug_trace", C.c_int, [C.c_void_p, C.c_int32]),
+    ("starkv_set_test_hooks", C.c_int, [C.c_int64, C.c_int32]),
+    ("starkv_quantize_split", C.c_int, [C.c_void_p, C.c_int32, C.c_int64, C.c_int32, C.c_int32, C.c_void_p,
+                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("starkv_decode_attention_static", C.c_int, [C.POINTER(Layout), C.POINTER(DecodeArgs), C.c_void_p]),
     ("starkv_static_scratch_bytes", C.c_size_t, []),
     ("starkv_static_read_device_error", C.c_int, [C.POINTER(C.c_int), C.c_void_p]),

@@ -58,30 +58,70 @@ def apply_rotary_pos_emb_custom(x, cos, sin, unsqueeze_dim=1):
     return (x * cos) + (rotate_half(x) * sin)
 
 
-class StarKVCache:
+try:                                                    # transformers' cache base class (the model code's type)
+    from transformers.cache_utils import Cache as _HFCache
+except Exception:                                       # pragma: no cover - transformers absent
+    _HFCache = object
+
+
+class StarKVCache(_HFCache):
     """Preallocated per-layer latent caches (the static replacement of the
-    reference's ``DynamicCache`` for the drop-in modules).
+    reference's ``DynamicCache`` for the drop-in modules).  A transformers
+    ``Cache``: pass it as ``past_key_values`` to ``LlamaModel`` /
+    ``LlamaForCausalLM.forward`` (as the reference's latency harness does with
+    its caches, latency.py:69-99) and the drop-in modules append each step's
+    latents in place.
 
     capacity: token slots per sequence; quantized: int8 K / int4 V codes."""
 
     def __init__(self, capacity: int, quantized: bool = False):
+        if _HFCache is not object:
+            super().__init__(layers=[])
         self.capacity = int(capacity)
         self.quantized = bool(quantized)
-        self.layers: Dict[int, DecodeLayer] = {}
+        self.states: Dict[int, DecodeLayer] = {}
 
+    # ---- the Cache interface the transformers model code uses
     def get_seq_length(self, layer_idx: int = 0) -> int:
-        st = self.layers.get(layer_idx)
+        st = self.states.get(layer_idx)
+        if st is None and self.states:
+            st = next(iter(self.states.values()))
         return 0 if st is None else st.length
 
+    def get_mask_sizes(self, query_length: int, layer_idx: int = 0):
+        return self.get_seq_length(layer_idx) + query_length, 0
+
+    def get_max_cache_shape(self, layer_idx: int = 0) -> int:
+        return self.capacity
+
+    @property
+    def is_compileable(self) -> bool:
+        return False
+
+    @property
+    def is_initialized(self) -> bool:
+        return bool(self.states)
+
+    @property
+    def is_sliding(self):
+        return [False] * max(1, len(self.states))
+
+    def __len__(self):
+        return len(self.states)
+
+    def update(self, key_states, value_states, layer_idx, *args, **kwargs):
+        raise NotImplementedError("StarKVCache is written by the STAR-KV attention modules themselves "
+                                  "(latents appended in place by the decode kernels)")
+
     def layer(self, layer_idx: int, module: "LlamaCustomAttention", batch: int, dtype: torch.dtype) -> DecodeLayer:
-        st = self.layers.get(layer_idx)
+        st = self.states.get(layer_idx)
         if st is None:
             v_ranks, v_kv = module.v_blocks()
             lay = ops.make_layout(batch, module.num_heads, module.num_key_value_heads, module.k_ranks(),
                                   v_ranks, v_kv, self.capacity, self.quantized, dtype)
             st = DecodeLayer(lay, module.packed_k_u(dtype), module.v_proj.U.weight.to(dtype).contiguous(),
                              module.rope_theta)
-            self.layers[layer_idx] = st
+            self.states[layer_idx] = st
         return st
 
 
@@ -266,6 +306,8 @@ class LlamaCustomAttentionQuant(LlamaCustomAttention):
                 past_key_values_upper=None, past_key_values_lower=None, scales_upper=None, scales_lower=None,
                 cache_position=None, **kwargs):
         cache = past_key_values_upper
+        if cache is None:                                # called by transformers' decoder layer
+            cache = kwargs.pop("past_key_values", None)
         if cache is not None and not isinstance(cache, StarKVCache):
             raise TypeError("the quantised module takes a StarKVCache(quantized=True) as past_key_values_upper")
         if cache is not None and not cache.quantized:

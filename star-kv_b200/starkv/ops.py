@@ -56,9 +56,16 @@ def _require(t: torch.Tensor, name: str, dtype=None, numel=None, align=16):
 def make_layout(batch: int, num_q_heads: int, num_kv_heads: int, k_ranks: Sequence[int],
                 v_ranks: Sequence[int], v_block_kv: Sequence[int], capacity: int, quantized: bool,
                 latent_dtype: torch.dtype, k_offsets: Optional[Sequence[int]] = None,
-                k_batch_strides: Optional[Sequence[int]] = None) -> Layout:
+                k_batch_strides: Optional[Sequence[int]] = None, k_tiled: Optional[bool] = None) -> Layout:
     """Build a ``starkv_layout``.  Default K layout: head h is a contiguous
-    (B, capacity, r_h) region at offset B*capacity*sum(r_<h)."""
+    (B, capacity, r_h) region at offset B*capacity*sum(r_<h), tiled (128-slot
+    tiles of 16-byte column chunks) with the capacity rounded up to a multiple
+    of 128.  Explicit offsets / strides (the reference's (B, Hkv, L, r) tensor)
+    default to the row-major layout."""
+    if k_tiled is None:
+        k_tiled = k_offsets is None and k_batch_strides is None
+    if k_tiled:
+        capacity = (capacity + 127) // 128 * 128
     L = Layout()
     L.abi_version = _lib.ABI_VERSION
     L.batch, L.num_q_heads, L.num_kv_heads, L.head_dim = batch, num_q_heads, num_kv_heads, 128
@@ -66,6 +73,7 @@ def make_layout(batch: int, num_q_heads: int, num_kv_heads: int, k_ranks: Sequen
     L.capacity = capacity
     L.quantized = int(bool(quantized))
     L.latent_dtype = dtype_code(latent_dtype)
+    L.k_tiled = int(bool(k_tiled))
     col = 0
     for h, r in enumerate(k_ranks):
         L.k_rank[h] = r
@@ -172,11 +180,16 @@ class LatentCache:
 
     # ---- host views for tests / export
     def k_head(self, h: int) -> torch.Tensor:
-        """(B, capacity, r_h) view of KV head h."""
+        """(B, capacity, r_h) row-major copy (tiled layout) or view (row-major) of KV head h."""
         L = self.layout
         r = L.k_rank[h]
         n = L.batch * L.capacity * r
-        return self.k_cache[L.k_offset[h]:L.k_offset[h] + n].view(L.batch, L.capacity, r)
+        flat = self.k_cache[L.k_offset[h]:L.k_offset[h] + n]
+        if not L.k_tiled:
+            return flat.view(L.batch, L.capacity, r)
+        per = 16 // flat.element_size()
+        t = flat.view(L.batch, L.capacity // 128, r // per, 128, per)
+        return t.permute(0, 1, 3, 2, 4).reshape(L.batch, L.capacity, r)
 
 
 _WORKSPACES = {}
@@ -287,7 +300,8 @@ def k_logits(layout: Layout, cache: LatentCache, q: torch.Tensor, k_u: torch.Ten
     B, Hq = layout.batch, layout.num_q_heads
     logits = torch.empty(B, Hq, num_tokens, dtype=torch.float32, device=q.device)
     _require(inv_freq, "inv_freq", torch.float32, 64, align=4)
-    a = _decode_args(layout, cache, q, k_u, None, inv_freq, 1.0, num_tokens, None, None, None, num_splits)
+    ws = workspace(workspace_size(layout, num_tokens, num_splits), q.device)
+    a = _decode_args(layout, cache, q, k_u, None, inv_freq, 1.0, num_tokens, None, None, ws, num_splits)
     check(load().starkv_k_logits(C.byref(layout), C.byref(a), _ptr(logits), _stream()), "starkv_k_logits")
     return logits
 
@@ -300,6 +314,34 @@ def v_latent(layout: Layout, cache: LatentCache, probs: torch.Tensor, num_tokens
     check(load().starkv_v_latent(C.byref(layout), _ptr(probs), num_tokens, _ptr(cache.v_cache),
                                  _ptr(cache.v_params), _ptr(out), _stream()), "starkv_v_latent")
     return out
+
+
+def quantize_split(x: torch.Tensor, split_r: int):
+    """The reference's split quantiser (``starkv_quantize_split``): x (..., r) ->
+    (up_q int8 (..., split_r), s_up fp16 (..., 1), lo_q uint8 (..., ceil(r4/2)),
+    s_lo fp16 (..., 1), r4 = r - split_r)."""
+    if not x.is_cuda:
+        raise _lib.StarKVError("quantize_split takes CUDA tensors")
+    x = x.contiguous()
+    r = x.shape[-1]
+    split_r = min(int(split_r), r)
+    r4 = r - split_r
+    lead = x.shape[:-1]
+    rows = x.numel() // r if r else 0
+    up = torch.empty(*lead, split_r, dtype=torch.int8, device=x.device)
+    s_up = torch.ones(*lead, 1, dtype=torch.float16, device=x.device)
+    lo = torch.empty(*lead, (r4 + 1) // 2, dtype=torch.uint8, device=x.device)
+    s_lo = torch.ones(*lead, 1, dtype=torch.float16, device=x.device)
+    check(load().starkv_quantize_split(_ptr(x), dtype_code(x.dtype), rows, r, split_r, _ptr(up) if split_r else None,
+                                       _ptr(s_up), _ptr(lo) if r4 else None, _ptr(s_lo), _stream()),
+          "starkv_quantize_split")
+    return up, s_up, lo, s_lo, r4
+
+
+def set_test_hooks(wait_limit_ns: int = 0, skip_copy_unit: int = -1):
+    """Test hooks of the device failure path (``starkv_set_test_hooks``); no
+    arguments restore normal operation."""
+    check(load().starkv_set_test_hooks(int(wait_limit_ns), int(skip_copy_unit)), "starkv_set_test_hooks")
 
 
 def read_device_error(ws: Optional[torch.Tensor] = None, device="cuda") -> int:

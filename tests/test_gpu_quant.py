@@ -59,6 +59,7 @@ def test_append_saturates_and_handles_constant_groups(cuda):
 def test_append_rejects_overflow(cuda):
     spec = make_spec("c1", seed=5, num_q_heads=4, batch=1, context=10)
     st = build_step(make_layer(spec), cuda)
-    st.layer.append(st.k_new, st.v_new)              # fills the last slot (capacity = tokens)
+    st.layer.cache.length = st.layer.layout.capacity - 1   # capacity: tokens rounded up to a 128-slot tile
+    st.layer.append(st.k_new, st.v_new)                    # fills the last slot
     with pytest.raises(ops._lib.StarKVError):
         st.layer.append(st.k_new, st.v_new)
