@@ -247,8 +247,8 @@ int starkv_quantize_split(const void* x, int32_t dtype, int64_t rows, int32_t r,
 /*
  * Test hooks for the device-side failure path (no counterpart in the
  * reference): wait_limit_ns (> 0; 0 restores the default 2 s) bounds every
- * mbarrier wait of the K kernel; skip_copy_unit >= 0 makes the K kernel's
- * first CTA never issue that unit's staging copy, so that its consumers' waits
+ * mbarrier wait of the K kernel; skip_copy_unit >= 0 makes the K kernel
+ * never issue the staging copy of that unit of its work stream, so that its consumers' waits
  * run out, record an error code in the workspace's first word and return.
  * (0, -1) restores normal operation.  Not for production use.
  */

@@ -27,8 +27,8 @@
 //   converter warpgroups (2, alternate units): thread = token row; reads its
 //                    row's 16-byte chunks (conflict-free with the tiled cache
 //                    layout), converts to fp16 (int8 codes are exact) and writes
-//                    the A operand into a ring of four 32-column TMEM slots (a
-//                    unit takes one slot per 64 ranks);
+//                    the A operand into a ring of TMEM slots (four of 32
+//                    columns when every rank is <= 64, else two of 64);
 //   MMA issuers (2, alternate units): per job r/16 tcgen05.mma (A from TMEM,
 //                    B = W from shared memory, M=128, N=128, K=16) into
 //                    accumulator j mod 3;
@@ -76,13 +76,14 @@ struct KParams {
   const uint8_t* wpre;    // W of every (sequence, query head) from k_wprep_kernel (stride wstride)
   const float* weta;      // its power-of-two normalisation per (sequence, query head)
   int wstride;            // bytes per (sequence, query head) W image
+  int rmax;               // largest K rank of the layout
   int G;                  // KV heads per group: the jobs of a group's tile share one RoPE rotation
   int cost[STARKV_MAX_KV_HEADS];  // scheduling cost of one unit of each KV head
   long long cost_seq;     // sum over KV heads of cost * ntiles: the cost of one sequence
   unsigned long long wait_ns;  // time limit of one device wait
   int ref_angles;         // 1: round each RoPE angle like the reference, fl(l * w_i) in fp32 (long contexts;
                           //    selects the REF instance of k_stream_kernel)
-  int skip_unit;          // test hook: CTA 0's producer never issues this unit's copy (-1: off)
+  int skip_unit;          // test hook: the copy of this stream unit is never issued (-1: off)
 #ifdef STARKV_KTRACE
   long long* trace;       // diagnostic builds only: clock64 per (job of CTA 0, field)
 #endif
@@ -105,7 +106,7 @@ constexpr int kKThreads = 640;
 // drains (48 + 2*64 + 2*152 = 480 <= 5 * 96, the launch budget).
 constexpr int kKCtlRegs = 56, kKConvRegs = 56, kKDrainRegs = 152;
 constexpr int kKAcc = 3;         // accumulators in TMEM (columns [0, 384))
-constexpr int kKASlots = 4;      // A ring slots of 32 TMEM columns (columns [384, 512))
+constexpr int kKASlots = 4;      // A ring slots (at most), TMEM columns [384, 512)
 constexpr int kKHeader = 8192;   // barriers, rotations and the partial-sum ring at the start of dynamic smem
 constexpr int kKSmemMax = 227 * 1024;
 constexpr int kKMaxStages = 32;
@@ -369,8 +370,12 @@ __global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_con
   constexpr int CPC = 8 / XB;                              // TMEM columns (fp16 pairs) per 16-byte chunk
   constexpr int PCH = (32 / CPC) < 8 ? (32 / CPC) : 8;     // chunks per conversion piece (<= 32 columns)
   const bool tiled = lay.k_tiled != 0;
-
-  // ---- shared memory carve-up
+  // A ring: four 32-column slots when every rank is <= 64 (r fp16 per row = r / 2
+  // columns), else two of 64.  Unit i takes slot i % nAs; since the converter
+  // warpgroups, and the issuers, alternate units, every slot is always written
+  // by the same warpgroup and read by the same issuer, so each waits its slot's
+  // phases strictly in order.
+  const int nAs = p.rmax <= 64 ? 4 : 2, aW = 128 / nAs;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
   uint64_t* st_full = bars;                   // [32] staging slot landed (tx bytes)
   uint64_t* st_empty = bars + 32;             // [32] staging slot read (4 converter warps)
@@ -433,11 +438,25 @@ __global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_con
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int u0 = s_range[0], u1 = s_range[1];
+#ifdef STARKV_KTRACE
+  if (p.trace && tid == 0) {
+    p.trace[kKTraceJobs * kKTraceFields + blockIdx.x * 4 + 0] = (long long)global_timer_ns();
+    p.trace[kKTraceJobs * kKTraceFields + blockIdx.x * 4 + 2] = u1 - u0;
+  }
+#endif
   const unsigned long long wlim = p.wait_ns;
-  auto fail = [&](int code) {
+  auto fail_at = [&](int code, int line) {
     record_error(p.err, code);
     *s_abort = 1;
+#ifdef STARKV_KTRACE
+    if (p.trace)
+      atomicCAS(reinterpret_cast<unsigned long long*>(p.trace + kKTraceJobs * kKTraceFields + blockIdx.x * 4 + 3), 0ull,
+                (unsigned long long)line);
+#else
+    (void)line;
+#endif
   };
+#define fail(code) fail_at(code, __LINE__)
   const int NS = p.nstage;
 
   if (wg == 0) {
@@ -470,7 +489,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_con
           }
           const int s = i % NS;
           if (!mbar_wait(st_empty + s, (uint32_t)(((i / NS) & 1) ^ 1), wlim)) { fail(kDevWaitCopy); break; }
-          if (i == p.skip_unit && blockIdx.x == 0) continue;   // test hook: this stage never lands
+          if (it.u == p.skip_unit) continue;                   // test hook: this stage never lands
           const int t0 = it.tile * 128;
           const uint32_t bytes = (uint32_t)((tiled ? 128 : min(128, p.T - t0)) * R);
           const uint8_t* src = reinterpret_cast<const uint8_t*>(p.k_cache) +
@@ -482,7 +501,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_con
         // every copy issued has landed before the CTA may exit (each wait bounded;
         // a stage that was never issued only costs its time limit)
         for (int k = max(0, i - NS); k < i; ++k)
-          if (!(k == p.skip_unit && blockIdx.x == 0) && !mbar_wait(st_full + k % NS, (uint32_t)((k / NS) & 1), wlim))
+          if (!(u0 + k == p.skip_unit) && !mbar_wait(st_full + k % NS, (uint32_t)((k / NS) & 1), wlim))
             fail(kDevWaitCopy);
         for (int k = max(0, nseg - p.nW); k < nseg; ++k)
           if (!mbar_wait(w_full + k % p.nW, (uint32_t)((k / p.nW) & 1), wlim)) fail(kDevWaitCopy);
@@ -493,30 +512,32 @@ __global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_con
       // Issuer iw takes the units i with i % 2 == iw (one thread issues a
       // tcgen05.mma about as fast as the tensor core retires one, so two keep it
       // busy); both walk every unit to follow the job, A-ring and W offsets.
+      // (With several jobs per unit one issuer keeps the tensor core busy, and
+      // two could run one accumulator phase ahead of the drains.)
       const int iw = warp - 1;
-      if (lane == 0) {
+      const int NI = qpk == 1 ? 2 : 1;                       // issuers
+      if (lane == 0 && iw < NI) {
         constexpr uint32_t IDESC = idesc_f16_f32(128, 128);
         KUnitIter it;
         it.init(u0, u1, p.ntiles, Hkv, G);
-        int apos = 0, j = 0;
+        int j = 0;
         uint32_t woff = 0;                                  // byte offset of this KV head's W images in the slot
         bool ok = true;
         for (int i = 0; it.valid() && ok; it.next(), ++i) {
           if (*s_abort) break;
-          const int r = lay.k_rank[it.kv], na = (r + 63) >> 6;
+          const int r = lay.k_rank[it.kv];
           const int ws = it.seg % p.nW;
+          const int as = i % nAs;                              // A slot of unit i, used for the (i / nAs)-th time
           if (it.tfirst) {
             woff = 0;
             for (int gk = 0; gk < it.gk; ++gk) woff += (uint32_t)(qpk * lay.k_rank[it.grp * G + gk] * 256);
           }
-          if ((i & 1) == iw) {
+          if (i % NI == iw) {
             if (it.first && !mbar_wait(w_full + ws, (uint32_t)((it.seg / p.nW) & 1), wlim)) { ok = false; break; }
-            for (int m = 0; m < na && ok; ++m)
-              if (!mbar_wait(a_full + ((apos + m) & 3), (uint32_t)(((apos + m) >> 2) & 1), wlim)) ok = false;
-            if (!ok) break;
+            if (!mbar_wait(a_full + as, (uint32_t)((i / nAs) & 1), wlim)) { ok = false; break; }
             tc_fence_after();
             KTRACE(j, 4);
-            const uint32_t acol = (uint32_t)(apos & 3) * 32u;
+            const uint32_t acol = 384u + (uint32_t)(as * aW);
             for (int g = 0; g < qpk; ++g) {
               const int jj = j + g;
               if (jj >= kKAcc && !mbar_wait(d_empty + jj % kKAcc, (uint32_t)(((jj / kKAcc) - 1) & 1), wlim)) { ok = false; break; }
@@ -526,20 +547,21 @@ __global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_con
                                                (uint32_t)r * 16u);
               const uint32_t d = tmem + (uint32_t)(jj % kKAcc) * 128u;
               for (int kk = 0; kk < (r >> 4); ++kk)
-                mma_f16_ts(d, tmem + 384u + ((acol + 8u * kk) & 127u), bdesc + (uint64_t)(kk * 16), IDESC, kk ? 1u : 0u);
+                mma_f16_ts(d, tmem + acol + 8u * kk, bdesc + (uint64_t)(kk * 16), IDESC, kk ? 1u : 0u);
               mma_commit(d_full + jj % kKAcc);
               KTRACE(jj, 6);
             }
             if (!ok) break;
-            for (int m = 0; m < na; ++m) mma_commit(a_empty + ((apos + m) & 3));
+            mma_commit(a_empty + as);
           }
-          if (it.last_of_seg()) mma_commit(w_empty + ws);  // both issuers: the slot is free once both retired
+          if (it.last_of_seg())                             // every issuer: the slot is free once all retired
+            for (int k = NI; k <= 2; ++k) mma_commit(w_empty + ws);
           woff += (uint32_t)(qpk * r * 256);
-          apos += na;
           j += qpk;
         }
         if (!ok) fail(kDevWaitMma);
         mma_commit(fin_bar);                     // arrives once every MMA of this thread retired
+        if (NI == 1) mma_commit(fin_bar);
         if (!mbar_wait(fin_bar, 0, wlim)) fail(kDevWaitMma);
       }
       __syncwarp();
@@ -554,29 +576,30 @@ __global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_con
     const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
     KUnitIter it;
     it.init(u0, u1, p.ntiles, Hkv, G);
-    int apos = 0;
     for (int i = 0; it.valid(); it.next(), ++i) {
-      const int r = lay.k_rank[it.kv], na = (r + 63) >> 6;
+      const int r = lay.k_rank[it.kv];
+      const int as = i % nAs;
       if ((i & 1) == cw) {
         if (*s_abort) break;
         const int s = i % NS;
         if (!mbar_wait(st_full + s, (uint32_t)((i / NS) & 1), wlim)) { fail(kDevWaitCopy); break; }
         if (row == 0) KTRACE(i, 1);
-        bool ok = true;
-        for (int m = 0; m < na && ok; ++m)
-          if (!mbar_wait(a_empty + ((apos + m) & 3), (uint32_t)((((apos + m) >> 2) & 1) ^ 1), wlim)) ok = false;
-        if (!ok) { fail(kDevWaitMma); break; }
-        tc_fence_after();
-        if (row == 0) KTRACE(i, 2);
         const int R = r * XB, nch = R >> 4;
         const int cs = tiled ? 2048 : 16;
         const uint8_t* srow = Ssm + (size_t)s * p.stage_bytes + (tiled ? row * 16 : row * R);
-        const uint32_t acol = (uint32_t)(apos & 3) * 32u;
-        for (int c0 = 0; c0 < nch; c0 += PCH) {
-          uint32_t o[32];
+        const uint32_t acol = 384u + (uint32_t)(as * aW);
+        // the first piece is converted before the A slots are free (its latency
+        // overlaps the wait), the rest after
+        uint32_t o[32];
+        k_convert_piece<XT, PCH>(srow, cs, min(PCH, nch), o);
+        if (!mbar_wait(a_empty + as, (uint32_t)(((i / nAs) & 1) ^ 1), wlim)) { fail(kDevWaitMma); break; }
+        tc_fence_after();
+        if (row == 0) KTRACE(i, 2);
+        tmem_st_cols(lane_base + acol, o, min(PCH, nch) * CPC);
+        for (int c0 = PCH; c0 < nch; c0 += PCH) {
           const int n = min(PCH, nch - c0);
           k_convert_piece<XT, PCH>(srow + c0 * cs, cs, n, o);
-          tmem_st_cols(lane_base + 384u + ((acol + (uint32_t)(c0 * CPC)) & 127u), o, n * CPC);
+          tmem_st_cols(lane_base + acol + (uint32_t)(c0 * CPC), o, n * CPC);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(st_empty + s);            // the stage is read: back to the producer
@@ -584,10 +607,9 @@ __global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_con
         tc_fence_before();
         __syncwarp();
         if (lane == 0)
-          for (int m = 0; m < na; ++m) mbar_arrive(a_full + ((apos + m) & 3));
-        if (row == 0) KTRACE(i, 3);
+          mbar_arrive(a_full + as);
+        if (lane == 0) KTRACE(i, (row >> 5) == 0 ? 3 : 12 + (row >> 5));
       }
-      apos += na;
     }
   } else {
     // ============================================================ drain warpgroups
@@ -754,10 +776,14 @@ __global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_con
   // the producer waited the last stages)
   tc_fence_before();
   __syncthreads();
+#ifdef STARKV_KTRACE
+  if (p.trace && tid == 0) p.trace[kKTraceJobs * kKTraceFields + blockIdx.x * 4 + 1] = (long long)global_timer_ns();
+#endif
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+#undef fail
 }
 
 }  // namespace starkv

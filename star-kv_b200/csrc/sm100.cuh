@@ -86,21 +86,30 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns false
-// (and leaves the barrier alone) when limit_ns passes first.  try_wait blocks for a
-// hardware-defined window; the timer is read every 64 windows, and long waits back
-// off so that waiting warps leave issue slots to working ones.
+// (and leaves the barrier alone) when limit_ns passes first.  try_wait with a
+// suspend-time hint puts the waiting warp to sleep in hardware until the phase
+// completes (or the hint runs out), so waiting warps take no issue slots from
+// working ones; the timer is checked between such sleeps.
+__device__ __forceinline__ bool mbar_try_wait_for(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           unsigned long long limit_ns = kWaitLimitNs) {
-  if (mbar_try_wait_plain(bar, parity)) return true;
+  if (mbar_try_wait_for(bar, parity, 20000u)) return true;
   const unsigned long long t0 = global_timer_ns();
 #pragma unroll 1
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait_plain(bar, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (global_timer_ns() - t0 > limit_ns) return false;
-      __nanosleep(64);
-    }
-  }
+  while (!mbar_try_wait_for(bar, parity, 20000u))
+    if (global_timer_ns() - t0 > limit_ns) return false;
+  return true;
 }
 
 // ------------------------------------------------------- bulk async copies

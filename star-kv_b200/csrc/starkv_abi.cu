@@ -25,6 +25,7 @@ unsigned long long g_wait_ns = kWaitLimitNs;
 int g_skip_unit = -1;
 #ifdef STARKV_KTRACE
 long long* g_ktrace = nullptr;
+long long* g_vtrace = nullptr;
 #endif
 
 int fail_launch() {
@@ -357,6 +358,7 @@ int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp
   kp.ntiles = (a->num_tokens + 127) / 128;
   kp.nW = g.nW;
   kp.G = g.G;
+  kp.rmax = g.rmax;
   kp.wslot_bytes = g.wslot;
   kp.nstage = g.nstage;
   kp.stage_bytes = g.stage_bytes;
@@ -605,6 +607,9 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
     v2.nstages = vg.nstages;
     v2.stage_bytes = vg.stage_bytes;
     v2.b_bytes = vg.b_bytes;
+#ifdef STARKV_KTRACE
+    v2.trace = g_vtrace;
+#endif
     rc = vg.np == 16 ? launch_v2<16>(v2, vg, st) : launch_v2<32>(v2, vg, st);
   } else {
     VParams vp;
@@ -689,6 +694,10 @@ int starkv_v_latent(const starkv_layout* lay, const float* probs, int32_t num_to
 // Diagnostic builds only (not declared in starkv.h): K-kernel timeline buffer.
 int starkv_debug_ktrace(void* buf) {
   g_ktrace = reinterpret_cast<long long*>(buf);
+  return STARKV_OK;
+}
+int starkv_debug_vtrace(void* buf) {
+  g_vtrace = reinterpret_cast<long long*>(buf);
   return STARKV_OK;
 }
 #endif

@@ -446,7 +446,18 @@ struct V2Params {
   int* err;
   int T, nsplit, nsplit_k, tps, rv_max;
   int nstages, stage_bytes, b_bytes;
+#ifdef STARKV_KTRACE
+  long long* trace;      // diagnostic builds only: clock64 per (tile of CTA (0, 0), field)
+#endif
 };
+#ifdef STARKV_KTRACE
+#define VTRACE(t, f)                                                                                   \
+  do {                                                                                                 \
+    if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && (t) < 256) p.trace[(t) * 8 + (f)] = clock64(); \
+  } while (0)
+#else
+#define VTRACE(t, f) do { } while (0)
+#endif
 
 
 __host__ __device__ inline int v2_stage_bytes(int R) {
@@ -623,6 +634,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         mbar_arrive_expect_tx(st_full + s, cb + pb);
         uint8_t* dst = Ssm + (size_t)s * p.stage_bytes;
         bulk_g2s(dst, p.v_cache + row0 * code_row, cb, st_full + s);
+        VTRACE(t, 0);
         if (pb) bulk_g2s(dst + kV2Tile * code_row, p.v_params + pa, pb, st_full + s);
         // the tile's logits (one row of nrows floats per head) into L2 for the prob
         // warps: the 16-byte-aligned span inside each row (a hint; the ends are
@@ -647,6 +659,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         if (*s_abort) break;
         const int tb = t & 1;
         if (!mbar_wait(b_full + tb, (uint32_t)((t >> 1) & 1))) { ok = false; break; }
+        VTRACE(t, 3);
         const uint32_t bt = smem_u32(Bsm + tb * p.b_bytes);
         for (int m = 0; m < MU; ++m, ++mc) {
           const int k = mc % kV2Abufs;
@@ -661,6 +674,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
           mma_commit(a_empty + k);
         }
         mma_commit(b_empty + tb);
+        VTRACE(t, 4);
       }
       if (!ok) fail(kDevWaitMma);
       mma_commit(fin_bar);
@@ -727,6 +741,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(b_full + tb);
+      if (tid == 64) VTRACE(t, 2);
     }
     if (!ok) fail(kDevWaitMma);
     // sum over the 4 lanes of a head (same lane & 7), then over the two warps
@@ -752,6 +767,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       if (*s_abort) break;
       const int s = t % NS;
       if (!mbar_wait(st_full + s, (uint32_t)((t / NS) & 1))) { ok = false; break; }
+      if (dw == 0 && lane == 0) VTRACE(t, 1);
       const uint8_t* codes = Ssm + (size_t)s * p.stage_bytes;
       const uint8_t* pars = codes + kV2Tile * code_row;
       const int t0 = t_begin + t * kV2Tile;
@@ -781,6 +797,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       }
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(st_empty + s);
+      if (dw == 0 && lane == 0) VTRACE(t, 5);
     }
     if (!ok) fail(kDevWaitMma);
     // ---- epilogue: accumulators -> split partials (warp quarter = TMEM lanes)
