@@ -164,8 +164,7 @@ typedef struct starkv_decode_args {
   const void* v_params;
   void* out;                /* (B, Hq, 128) out_dtype */
   int32_t out_dtype;
-  int32_t num_splits;       /* sequence splits of the V pass per sequence; 0 = automatic (the K pass
-                               balances its own work over the SMs) */
+  int32_t num_splits;       /* sequence splits per (sequence, head group); 0 = automatic */
   void* workspace;          /* scratch, 256-byte aligned */
   size_t workspace_bytes;
   void* const* events;      /* optional: 4 cudaEvent_t recorded on the stream before the K kernel, after
@@ -176,7 +175,7 @@ typedef struct starkv_decode_args {
 int starkv_decode_workspace_size(const starkv_layout* lay, int32_t num_tokens, int32_t num_splits,
                                  size_t* bytes);
 
-/* Number of V-pass sequence splits the automatic choice (num_splits = 0) uses. */
+/* Number of sequence splits the automatic choice (num_splits = 0) uses. */
 int32_t starkv_auto_splits(const starkv_layout* lay, int32_t num_tokens);
 
 /*
@@ -247,8 +246,9 @@ int starkv_quantize_split(const void* x, int32_t dtype, int64_t rows, int32_t r,
 /*
  * Test hooks for the device-side failure path (no counterpart in the
  * reference): wait_limit_ns (> 0; 0 restores the default 2 s) bounds every
- * mbarrier wait of the K kernel; skip_copy_unit >= 0 makes the K kernel
- * never issue the staging copy of that unit of its work stream, so that its consumers' waits
+ * mbarrier wait of the K kernel; skip_copy_unit >= 0 makes the K kernel's
+ * first CTA (split 0, head group 0, sequence 0) never issue that unit's staging
+ * copy, so that its consumers' waits
  * run out, record an error code in the workspace's first word and return.
  * (0, -1) restores normal operation.  Not for production use.
  */

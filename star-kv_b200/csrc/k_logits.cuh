@@ -12,47 +12,43 @@
 //     Q[c, i] = sc_c (q_{i+64} U[i, c] - q_i U[i+64, c])        (sc_c = K channel scale)
 // the whole K path is one GEMM  D = X_codes (tokens x r) @ W (r x 128)  on the
 // tensor cores followed by  logit_l = sum_i c_i D[l, i] + s_i D[l, 64 + i]  in the
-// TMEM drain.  The query is folded into W once per step (k_wprep_kernel), so
-// neither the keys nor the rotated keys are ever materialised.
+// TMEM drain.  The query is folded into W once per CTA, so neither the keys
+// nor the rotated keys are ever materialised.
 //
-// k_stream_kernel is persistent: one CTA per SM walks a contiguous range of the
-// unit stream (sequence b, KV head kv, 128-token tile), ordered b-major then kv
-// then tile.  The ranges are cut by an estimated cost per unit of each KV head
-// (HBM bytes, tensor-core and drain time), so that CTAs finish together however
-// ragged the ranks are.  A unit carries one job per query head of its KV head.
-// 640 threads, roles handing off through mbarriers (every wait bounded):
-//   producer warp:   the W images of a new (b, kv) segment and one 1-D bulk copy
-//                    per unit (a tile is one contiguous range in HBM) into a
-//                    ring of staging slots;
-//   converter warpgroups (2, alternate units): thread = token row; reads its
-//                    row's 16-byte chunks (conflict-free with the tiled cache
-//                    layout), converts to fp16 (int8 codes are exact) and writes
-//                    the A operand into a ring of TMEM slots (four of 32
-//                    columns when every rank is <= 64, else two of 64);
-//   MMA issuers (2, alternate units): per job r/16 tcgen05.mma (A from TMEM,
-//                    B = W from shared memory, M=128, N=128, K=16) into
-//                    accumulator j mod 3;
-//   drain warpgroups (2): each takes half of the 64 RoPE frequencies of every
-//                    job (32 cosine and 32 sine columns, two TMEM loads and one
-//                    wait, the accumulator released right after), the second
-//                    hands its partial sum to the first through shared memory,
-//                    which scales, masks, writes the fp32 logit and raises the
-//                    head's running maximum (one atomic per warp and job).
-// TMEM columns: [0, 384) three accumulators, [384, 512) the A ring.
+// CTA = (sequence split, group of G query heads, sequence b), 640 threads, one
+// CTA per SM (it owns the 512 TMEM columns).  A "unit" is one 128-token tile of
+// one KV head (the G heads form runs of heads that share a KV head); a "job" is
+// one (tile, query head) pair.  Roles, handing off through mbarriers (every wait
+// bounded):
+//   producer warp:   one 1-D bulk copy per unit (its rows are one contiguous
+//                    block in HBM) into a ring of tile slots in shared memory;
+//   converter warpgroups (2, alternate units): thread = token row; converts its
+//                    staged row (its 16-byte chunks 16 bytes apart in the
+//                    row-major layout, 2 KiB apart in the tiled one, where a
+//                    warp's reads are conflict-free) to fp16 (int8 codes are exact in fp16) into
+//                    registers, releases the stage, waits for its own A buffer in
+//                    TMEM and writes it with wide tcgen05.st — the A operand never
+//                    touches shared memory;
+//   MMA issuers (warps 1 and 2 for one-job units, else warp 1): per job r/16
+//                    tcgen05.mma (A from TMEM, B = W_g from shared memory, M=128,
+//                    N=128, K=16) into accumulator j mod 3;
+//   drain warpgroups (2, alternate tiles): thread = token row; eight 16-column
+//                    tcgen05.ld of the accumulator (released right after), the
+//                    RoPE-weighted sum over all 64 frequencies (packed fp32x2 FMA),
+//                    scale, mask, the logit to global and a running maximum per
+//                    head — the split maximum the V kernel's softmax starts from
+//                    (the V kernel forms the exponentials and their sums itself).
+// TMEM columns: [0, 384) three accumulators, [384, 512) two A buffers of 64
+// columns (r <= 128 fp16 values per row).
 //
-// RoPE angles: each drain thread owns one token row and the cos/sin of its 32
-// frequencies; they are exact (double-precision range reduction) at every 16th
-// tile of a sequence and advanced tile to tile by the exact rotation through
-// 128*w_i.  The values therefore depend only on the token position, not on how
-// the stream was cut into CTAs (sharded and unsharded runs agree bit for bit).
-// The reference's fp32 product fl(l*w_i) differs from the exact angle by at most
-// half an ulp of the angle; for long contexts (ref_angles) the drain applies that
-// rounding (first order in the difference, which an FMA gives exactly).
+// RoPE angles: each drain thread owns one token row; it starts from cos/sin of
+// l*w_i for the first token of its first tile and advances by the exact rotation
+// through 256*w_i to its next tile (fp32, packed FMAs, shared by the G heads of
+// the tile).  The angles are the exact l*w_i; the reference's fp32 product
+// fl(l*w_i) differs from them by at most half an ulp of the angle.
 #pragma once
 #include "common.cuh"
 #include "sm100.cuh"
-
-#include <type_traits>
 
 namespace starkv {
 
@@ -65,53 +61,40 @@ struct KParams {
   const float* inv_freq;  // (64,) fp32 RoPE inverse frequencies
   const float* mask;      // (B, T) additive or null
   float* logits;          // (B, Hq, T)
-  float* smax;            // (B, Hq) running maximum logit (reset by k_wprep_kernel), or null
+  float* smax;            // (B, Hq, nsplit) maximum logit of each split, or null
   int* err;
   int q_dtype, w_dtype;
-  int T, ntiles;          // tokens, 128-token tiles
-  int nW, wslot_bytes;    // W slots in shared memory, bytes per slot (qpk W images of rank rmax)
-  int nstage, stage_bytes;  // staging slots, bytes per slot (128 rows of rank rmax)
+  int T, nsplit, tps;     // tokens, splits, tokens per split (multiple of 128)
+  int G, rmax, bsum;      // heads per CTA, max rank, max per-group rank sum (W matrices in smem)
+  int stage_total;        // bytes of the staging ring
   float out_scale;        // multiplier of q.k (scaling * log2 e for decode)
   float mask_scale;       // multiplier of the mask (log2 e for decode)
-  const uint8_t* wpre;    // W of every (sequence, query head) from k_wprep_kernel (stride wstride)
-  const float* weta;      // its power-of-two normalisation per (sequence, query head)
+  const uint8_t* wpre;    // W of every (sequence, query head) from k_wprep_kernel (stride wstride), or null:
+  const float* weta;      //   then the CTA builds its W itself; eta of every (sequence, query head)
   int wstride;            // bytes per (sequence, query head) W image
-  int rmax;               // largest K rank of the layout
-  int G;                  // KV heads per group: the jobs of a group's tile share one RoPE rotation
-  int cost[STARKV_MAX_KV_HEADS];  // scheduling cost of one unit of each KV head
-  long long cost_seq;     // sum over KV heads of cost * ntiles: the cost of one sequence
   unsigned long long wait_ns;  // time limit of one device wait
-  int ref_angles;         // 1: round each RoPE angle like the reference, fl(l * w_i) in fp32 (long contexts;
-                          //    selects the REF instance of k_stream_kernel)
-  int skip_unit;          // test hook: the copy of this stream unit is never issued (-1: off)
-#ifdef STARKV_KTRACE
-  long long* trace;       // diagnostic builds only: clock64 per (job of CTA 0, field)
-#endif
+  int skip_unit;          // test hook: CTA (0, 0, 0) never issues this unit's copy (-1: off)
 };
-
-// Diagnostic timeline (built only with -DSTARKV_KTRACE): clock64 of CTA 0's first
-// kKTraceJobs jobs at each hand-off.
-#ifdef STARKV_KTRACE
-constexpr int kKTraceJobs = 1024, kKTraceFields = 16;
-#define KTRACE(job, field)                                                                  \
-  do {                                                                                      \
-    if (p.trace && blockIdx.x == 0 && (job) < kKTraceJobs) p.trace[(job) * kKTraceFields + (field)] = clock64(); \
-  } while (0)
-#else
-#define KTRACE(job, field) do { } while (0)
-#endif
 
 constexpr int kKThreads = 640;
 // Register budget per warpgroup after setmaxnreg: control, two converters, two
-// drains (48 + 2*64 + 2*152 = 480 <= 5 * 96, the launch budget).
-constexpr int kKCtlRegs = 56, kKConvRegs = 56, kKDrainRegs = 152;
+// drains (32 + 2*64 + 2*160 = 480 <= 5 * 96, the launch budget).
+constexpr int kKCtlRegs = 32, kKConvRegs = 64, kKDrainRegs = 160;
+constexpr int kKAbufs = 2;       // A buffers in TMEM (columns [384, 512)), one per converter warpgroup
 constexpr int kKAcc = 3;         // accumulators in TMEM (columns [0, 384))
-constexpr int kKASlots = 4;      // A ring slots (at most), TMEM columns [384, 512)
-constexpr int kKHeader = 8192;   // barriers, rotations and the partial-sum ring at the start of dynamic smem
+constexpr int kKHeader = 12288;  // barriers / scratch / partial-logit ring at the start of dynamic smem
 constexpr int kKSmemMax = 227 * 1024;
-constexpr int kKMaxStages = 32;
-constexpr int kKPart = 8;        // partial-sum slots (jobs in flight between the two drain warpgroups)
-constexpr int kKAnchor = 16;     // tiles between exact RoPE angles
+
+// Staging ring: a CTA's units are staged row-major (one bulk copy of 128 * R
+// contiguous bytes, R = r * element size) into tile slots; a tile slot holds the
+// units of every run of one 128-token tile back to back, and the ring has as
+// many tile slots as shared memory allows (at most kKMaxSlots unit slots).
+constexpr int kKMaxSlots = 32;
+
+// Staging bytes next to the W matrices of one CTA (one CTA per SM).
+__host__ __device__ inline long k_stage_total(int bsum) {
+  return ((long)kKSmemMax - kKHeader - (long)bsum * 256) & ~15L;
+}
 
 // 8 int8 codes -> 8 fp16 (exact): x -> (x + 128) as a byte; 0x64XX as fp16 is
 // 1024 + XX; subtract 1152.
@@ -126,15 +109,166 @@ __device__ __forceinline__ void cvt8_i8(uint32_t lo, uint32_t hi, uint32_t* o) {
   t = __byte_perm(b, 0x64646464u, 0x7362); h = __hsub2(*reinterpret_cast<__half2*>(&t), bias); o[3] = *reinterpret_cast<uint32_t*>(&h);
 }
 
+// TMEM columns (packed fp16 pairs) produced by one 16-byte staging chunk.
+template <typename XT>
+__host__ __device__ constexpr int k_cols_per_chunk() { return 8 / (int)sizeof(XT); }
+
+// Convert one 16-byte staging chunk to packed fp16 pairs and store them at
+// TMEM address `taddr` (this warp's lanes, consecutive columns).
+template <typename XT>
+__device__ __forceinline__ void cvt_store(const uint4 w, uint32_t taddr);
+
+template <>
+__device__ __forceinline__ void cvt_store<int8_t>(const uint4 w, uint32_t taddr) {
+  uint32_t o[8];
+  cvt8_i8(w.x, w.y, o);
+  cvt8_i8(w.z, w.w, o + 4);
+  tmem_st8(taddr, o);
+}
+template <>
+__device__ __forceinline__ void cvt_store<__half>(const uint4 w, uint32_t taddr) {
+  const uint32_t o[4] = {w.x, w.y, w.z, w.w};
+  tmem_st4(taddr, o);
+}
+template <>
+__device__ __forceinline__ void cvt_store<__nv_bfloat16>(const uint4 w, uint32_t taddr) {
+  const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float lo = __uint_as_float(in[k] << 16), hi = __uint_as_float(in[k] & 0xFFFF0000u);
+    __half2 h = __floats2half2_rn(lo, hi);
+    o[k] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  tmem_st4(taddr, o);
+}
+template <>
+__device__ __forceinline__ void cvt_store<float>(const uint4 w, uint32_t taddr) {
+  __half2 h0 = __floats2half2_rn(__uint_as_float(w.x), __uint_as_float(w.y));
+  __half2 h1 = __floats2half2_rn(__uint_as_float(w.z), __uint_as_float(w.w));
+  const uint32_t o[2] = {*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1)};
+  tmem_st2(taddr, o);
+}
+
+// Convert N staged chunks (loads first, then conversions and stores).
+template <typename XT, int N>
+__device__ __forceinline__ void convert_chunks(const uint8_t* srow, int cs, uint32_t taddr) {
+  uint4 w[N];
+#pragma unroll
+  for (int c = 0; c < N; ++c) w[c] = *reinterpret_cast<const uint4*>(srow + cs * c);
+#pragma unroll
+  for (int c = 0; c < N; ++c) cvt_store<XT>(w[c], taddr + c * k_cols_per_chunk<XT>());
+}
+
+// int8 row of RC chunks: loads, conversions into registers, then the fewest wide
+// TMEM stores (x32 / x16 / x8 columns), at most 4 chunks (32 columns) at a time.
+template <int N>
+__device__ __forceinline__ void convert_row_i8(const uint8_t* srow, int cs, uint32_t taddr) {
+  if constexpr (N > 4) {
+    convert_row_i8<4>(srow, cs, taddr);
+    convert_row_i8<N - 4>(srow + 4 * cs, cs, taddr + 32);
+  } else {
+    uint4 w[N];
+#pragma unroll
+    for (int c = 0; c < N; ++c) w[c] = *reinterpret_cast<const uint4*>(srow + cs * c);
+    uint32_t o[8 * N];
+#pragma unroll
+    for (int c = 0; c < N; ++c) {
+      cvt8_i8(w[c].x, w[c].y, o + 8 * c);
+      cvt8_i8(w[c].z, w[c].w, o + 8 * c + 4);
+    }
+    if constexpr (N == 4) {
+      tmem_st32(taddr, o);
+    } else {
+      int col = 0;
+      if constexpr (N >= 2) {
+        tmem_st16(taddr, o);
+        col = 16;
+      }
+      if constexpr (N & 1) tmem_st8(taddr + col, o + col);
+    }
+  }
+}
+
+// int8 row of RC <= 6 chunks converted into registers (two chunks loaded at a
+// time), and the stores of such a row (fewest wide tcgen05.st): the conversion
+// can run before the row's A buffer is free, the stores after.
+template <int RC>
+__device__ __forceinline__ void load_cvt_i8(const uint8_t* srow, int cs, uint32_t* o) {
+#pragma unroll
+  for (int c = 0; c < RC; c += 2) {
+    const uint4 w0 = *reinterpret_cast<const uint4*>(srow + cs * c);
+    uint4 w1 = make_uint4(0u, 0u, 0u, 0u);
+    if (c + 1 < RC) w1 = *reinterpret_cast<const uint4*>(srow + cs * (c + 1));
+    cvt8_i8(w0.x, w0.y, o + 8 * c);
+    cvt8_i8(w0.z, w0.w, o + 8 * c + 4);
+    if (c + 1 < RC) {
+      cvt8_i8(w1.x, w1.y, o + 8 * c + 8);
+      cvt8_i8(w1.z, w1.w, o + 8 * c + 12);
+    }
+  }
+}
+template <int RC>
+__device__ __forceinline__ void store_row_i8(uint32_t taddr, const uint32_t* o) {
+  int col = 0;
+#pragma unroll
+  for (; col + 32 <= 8 * RC; col += 32) tmem_st32(taddr + col, o + col);
+  if constexpr ((8 * RC) % 32 >= 16) {
+    tmem_st16(taddr + col, o + col);
+    col += 16;
+  }
+  if constexpr ((8 * RC) % 16 >= 8) tmem_st8(taddr + col, o + col);
+}
+
+// Convert, release the stage, wait for the A buffer, store: RC <= 6 int8 chunks.
+template <int RC, typename Release, typename WaitA>
+__device__ __forceinline__ bool convert_ahead_i8(const uint8_t* srow, int cs, uint32_t taddr, Release release,
+                                                 WaitA wait_a) {
+  uint32_t o[8 * RC];
+  load_cvt_i8<RC>(srow, cs, o);
+  release();
+  if (!wait_a()) return false;
+  store_row_i8<RC>(taddr, o);
+  return true;
+}
+
+// Convert a staged row of rc chunks into TMEM: int8 rows in one piece, other
+// element types in groups of 8 chunks, then the rest.
+template <typename XT>
+__device__ __forceinline__ void convert_row(int rc, const uint8_t* srow, int cs, uint32_t taddr) {
+  if constexpr (sizeof(XT) == 1) {
+    switch (rc) {
+      case 1: convert_row_i8<1>(srow, cs, taddr); return;
+      case 2: convert_row_i8<2>(srow, cs, taddr); return;
+      case 3: convert_row_i8<3>(srow, cs, taddr); return;
+      case 4: convert_row_i8<4>(srow, cs, taddr); return;
+      case 5: convert_row_i8<5>(srow, cs, taddr); return;
+      case 6: convert_row_i8<6>(srow, cs, taddr); return;
+      case 7: convert_row_i8<7>(srow, cs, taddr); return;
+      case 8: convert_row_i8<8>(srow, cs, taddr); return;
+      default: break;
+    }
+  }
+  int c = 0;
+  for (; c + 8 <= rc; c += 8) convert_chunks<XT, 8>(srow + cs * c, cs, taddr + c * k_cols_per_chunk<XT>());
+  const uint8_t* sr = srow + cs * c;
+  const uint32_t t = taddr + c * k_cols_per_chunk<XT>();
+  switch (rc - c) {
+    case 1: convert_chunks<XT, 1>(sr, cs, t); break;
+    case 2: convert_chunks<XT, 2>(sr, cs, t); break;
+    case 3: convert_chunks<XT, 3>(sr, cs, t); break;
+    case 4: convert_chunks<XT, 4>(sr, cs, t); break;
+    case 5: convert_chunks<XT, 5>(sr, cs, t); break;
+    case 6: convert_chunks<XT, 6>(sr, cs, t); break;
+    case 7: convert_chunks<XT, 7>(sr, cs, t); break;
+    default: break;
+  }
+}
+
 // cos/sin of the exact angle l*w (w an fp32 value): the product is exact in
 // double; it is reduced by the nearest multiple of 2*pi in double, and the
 // fp32 sine/cosine of the reduced angle (|x| <= pi) is taken.
-#ifdef STARKV_SINCOS_NOINLINE
-__device__ __noinline__
-#else
-__device__ __forceinline__
-#endif
-void exact_sincos(int l, float w, float& c, float& s) {
+__device__ __forceinline__ void exact_sincos(int l, float w, float& c, float& s) {
   const double a = (double)l * (double)w;
   const double k = rint(a * 0.15915494309189533577);          // a / (2 pi)
   const double red = fma(-k, 6.28318530717958647693, a);
@@ -233,9 +367,8 @@ __device__ __forceinline__ void build_w_head(const KParams& p, int b, int qh, co
   }
 }
 
-// Pre-pass: W and eta of every (sequence, query head) into the workspace (the K
-// kernel's producer bulk-copies them), and the per-head maximum reset.  grid (Hq, B),
-// 256 threads.
+// Pre-pass: W and eta of every (sequence, query head) into the workspace, so that
+// the K kernel's prologue is a bulk copy.  grid (Hq, B), 256 threads.
 template <bool QUANT>
 __global__ void __launch_bounds__(256) k_wprep_kernel(const __grid_constant__ KParams p, uint8_t* wout, float* eout) {
   __shared__ float qv[128];
@@ -246,188 +379,92 @@ __global__ void __launch_bounds__(256) k_wprep_kernel(const __grid_constant__ KP
   __syncthreads();
   float eta;
   build_w_head<QUANT, 256>(p, b, qh, qv, wout + ((int64_t)b * Hq + qh) * p.wstride, red, t, [] { __syncthreads(); }, eta);
-  if (t == 0) {
-    eout[(int64_t)b * Hq + qh] = eta;
-    if (p.smax) p.smax[(int64_t)b * Hq + qh] = kNegBig;   // the K kernel's running maximum starts here
-  }
+  if (t == 0) eout[(int64_t)b * Hq + qh] = eta;
 }
 
-// Units of the stream: segments s = (b, group of G KV heads), ordered b-major;
-// within a segment tile-major, then the group's KV heads:
-//     u = ((b * ngrp + grp) * ntiles + tile) * G + gk.
-// The G * qpk jobs of one tile share the drain's RoPE rotation.  First unit of
-// CTA c: the tile where the cumulative cost reaches c / gridDim.x of the total.
-__device__ __forceinline__ int k_unit_start(const KParams& p, int c) {
-  const int G = p.G, ngrp = p.lay.num_kv_heads / G;
-  const long long units = (long long)p.lay.batch * ngrp * p.ntiles * G;
-  if (c >= (int)gridDim.x) return (int)units;
-  const long long target = (long long)((double)p.cost_seq * p.lay.batch * c / gridDim.x);
-  const int b = (int)(target / p.cost_seq);
-  long long rem = target - (long long)b * p.cost_seq;
-  int grp = 0;
-  long long tc = 0;
-  for (;; ++grp) {
-    tc = 0;
-    for (int k = 0; k < G; ++k) tc += p.cost[grp * G + k];
-    if (grp + 1 == ngrp || rem < tc * p.ntiles) break;
-    rem -= tc * p.ntiles;
-  }
-  int tile = (int)(rem / tc);
-  if (tile >= p.ntiles) tile = p.ntiles - 1;
-  return (int)((((long long)b * ngrp + grp) * p.ntiles + tile) * G);
-}
-
-// Walks a CTA's units in order; every role keeps its own copy (32-bit unit
-// indices: the host checks that they fit).
-struct KUnitIter {
-  int u, u1;
-  int b, grp, tile, gk, kv, seg, ntiles, ngrp, G;
-  bool first;                          // first unit of a (b, group) segment in this CTA
-  bool tfirst;                         // first unit of a tile in this CTA
-  __device__ void init(int u0, int end, int nt, int hkv, int g) {
-    u = u0; u1 = end; ntiles = nt; G = g; ngrp = hkv / g; seg = 0; first = tfirst = true;
-    const int t = u0 / g;
-    gk = u0 - t * g;
-    const int s = t / nt;
-    tile = t - s * nt;
-    b = s / ngrp;
-    grp = s - b * ngrp;
-    kv = grp * G + gk;
-  }
-  __device__ bool valid() const { return u < u1; }
-  __device__ bool last_of_seg() const { return (tile == ntiles - 1 && gk == G - 1) || u + 1 == u1; }
-  __device__ void next() {
-    ++u;
-    first = tfirst = false;
-    if (++gk == G) {
-      gk = 0;
-      tfirst = true;
-      if (++tile == ntiles) {
-        tile = 0;
-        first = true;
-        ++seg;
-        if (++grp == ngrp) { grp = 0; ++b; }
-      }
-    }
-    kv = grp * G + gk;
-  }
-};
-
-// Store n (multiple of 4, <= 32) consecutive 32-bit TMEM columns of this warp's
-// lanes (register offsets stay compile-time constants).
-__device__ __forceinline__ void tmem_st_cols(uint32_t taddr, const uint32_t* o, int n) {
-  switch (n) {
-    case 32: tmem_st32(taddr, o); break;
-    case 28: tmem_st16(taddr, o); tmem_st8(taddr + 16, o + 16); tmem_st4(taddr + 24, o + 24); break;
-    case 24: tmem_st16(taddr, o); tmem_st8(taddr + 16, o + 16); break;
-    case 20: tmem_st16(taddr, o); tmem_st4(taddr + 16, o + 16); break;
-    case 16: tmem_st16(taddr, o); break;
-    case 12: tmem_st8(taddr, o); tmem_st4(taddr + 8, o + 8); break;
-    case 8: tmem_st8(taddr, o); break;
-    default: tmem_st4(taddr, o); break;
-  }
-}
-
-// Convert up to NCH staged 16-byte chunks of one row (chunk stride cs) into
-// packed fp16 pairs o[] (cols_per_chunk(XT) columns per chunk).
-template <typename XT, int NCH>
-__device__ __forceinline__ void k_convert_piece(const uint8_t* src, int cs, int nch, uint32_t* o) {
-#pragma unroll
-  for (int c = 0; c < NCH; ++c) {
-    if (c < nch) {
-      const uint4 w = *reinterpret_cast<const uint4*>(src + c * cs);
-      if constexpr (sizeof(XT) == 1) {
-        cvt8_i8(w.x, w.y, o + 8 * c);
-        cvt8_i8(w.z, w.w, o + 8 * c + 4);
-      } else if constexpr (std::is_same<XT, __half>::value) {
-        o[4 * c] = w.x; o[4 * c + 1] = w.y; o[4 * c + 2] = w.z; o[4 * c + 3] = w.w;
-      } else if constexpr (std::is_same<XT, __nv_bfloat16>::value) {
-        const uint32_t in[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          __half2 h = __floats2half2_rn(__uint_as_float(in[k] << 16), __uint_as_float(in[k] & 0xFFFF0000u));
-          o[4 * c + k] = *reinterpret_cast<uint32_t*>(&h);
-        }
-      } else {
-        __half2 h0 = __floats2half2_rn(__uint_as_float(w.x), __uint_as_float(w.y));
-        __half2 h1 = __floats2half2_rn(__uint_as_float(w.z), __uint_as_float(w.w));
-        o[2 * c] = *reinterpret_cast<uint32_t*>(&h0);
-        o[2 * c + 1] = *reinterpret_cast<uint32_t*>(&h1);
-      }
-    }
-  }
-}
-
-template <typename XT, bool REF>
-__global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_constant__ KParams p) {
+template <typename XT, bool QUANT, int G>
+__global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_constant__ KParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int wg = __shfl_sync(0xffffffffu, warp >> 2, 0);   // warpgroup 0..4 (warp-uniform)
+  const int split = blockIdx.x, grp = blockIdx.y, b = blockIdx.z;
   const starkv_layout& lay = p.lay;
-  const int Hq = lay.num_q_heads, Hkv = lay.num_kv_heads, qpk = Hq / Hkv;
-  const int G = p.G, GJ = G * qpk;                         // KV heads per group, jobs per tile
+  const int Hq = lay.num_q_heads, qpk = Hq / lay.num_kv_heads;
+  const int t_begin = split * p.tps;
+  const int t_end = min(p.T, t_begin + p.tps);
+  const int ntiles = t_end > t_begin ? (t_end - t_begin + 127) / 128 : 0;
   constexpr int XB = (int)sizeof(XT);
-  constexpr int CPC = 8 / XB;                              // TMEM columns (fp16 pairs) per 16-byte chunk
-  constexpr int PCH = (32 / CPC) < 8 ? (32 / CPC) : 8;     // chunks per conversion piece (<= 32 columns)
-  const bool tiled = lay.k_tiled != 0;
-  // A ring: four 32-column slots when every rank is <= 64 (r fp16 per row = r / 2
-  // columns), else two of 64.  Unit i takes slot i % nAs; since the converter
-  // warpgroups, and the issuers, alternate units, every slot is always written
-  // by the same warpgroup and read by the same issuer, so each waits its slot's
-  // phases strictly in order.
-  const int nAs = p.rmax <= 64 ? 4 : 2, aW = 128 / nAs;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* st_full = bars;                   // [32] staging slot landed (tx bytes)
-  uint64_t* st_empty = bars + 32;             // [32] staging slot read (4 converter warps)
-  uint64_t* a_full = bars + 64;               // [4]  A slot written (4 converter warps)
-  uint64_t* a_empty = bars + 68;              // [4]  A slot's MMAs retired (commit)
-  uint64_t* d_full = bars + 72;               // [3]  accumulator ready (commit)
-  uint64_t* d_empty = bars + 75;              // [3]  accumulator read (8 drain warps)
-  uint64_t* p_full = bars + 78;               // [8]  partial sum of a job written (4 warps of the other drain)
-  uint64_t* w_full = bars + 86;               // [2]  W slot landed (tx bytes)
-  uint64_t* w_empty = bars + 88;              // [2]  W slot's MMAs retired (one commit per issuer)
-  uint64_t* fin_bar = bars + 90;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 1024);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 1028);
-  int* s_range = reinterpret_cast<int*>(smem + 1040);               // [2] unit range of this CTA
-  float* s_esc = reinterpret_cast<float*>(smem + 1088);             // [2][8] logit scale of each job of the segment
-  float2* s_w = reinterpret_cast<float2*>(smem + 1280);             // [32] inverse frequencies (2i, 2i+1)
-  float4* s_rot = reinterpret_cast<float4*>(smem + 1536);           // [32] rotation by one tile
-  float* s_part = reinterpret_cast<float*>(smem + 2048);            // [8][128]
-  uint8_t* Wsm = smem + kKHeader;
-  uint8_t* Ssm = Wsm + (size_t)p.nW * p.wslot_bytes;
+  const bool tiled = lay.k_tiled != 0;                   // tiles stored as 16-byte column chunks (starkv.h)
+  const unsigned long long wlim = p.wait_ns;
+
+  // ---- shared memory carve-up
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 8192);
+  uint64_t* st_full = bars;                      // [32] unit slot landed (tx bytes)
+  uint64_t* st_empty = bars + 32;                // [32] unit slot read by the 4 converter warps
+  uint64_t* a_full = bars + 64;                  // [2]  A buffer written (4 converter warps)
+  uint64_t* a_empty = bars + 80;                 // [2]  A buffer's MMAs retired (commit)
+  uint64_t* d_full = bars + 96;                  // [6G] job slot j % 6G: accumulator j % 3 ready (commit)
+  uint64_t* d_empty = bars + 120;                // [6G] job slot j % 6G: accumulator read by the job's 4 drain warps
+  uint64_t* fin_bar = bars + 144;
+  uint64_t* w_bar = bars + 145;                  // W images landed (pre-pass mode)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 512);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 516);
+  int* s_nruns = reinterpret_cast<int*>(smem + 520);
+  int* s_boff = reinterpret_cast<int*>(smem + 528);           // [4] byte offset of W_g
+  int* s_rank = reinterpret_cast<int*>(smem + 544);           // [4] rank of head g
+  const uint8_t** s_src = reinterpret_cast<const uint8_t**>(smem + 640);  // [4] latents of (b, kv(g)) at slot 0
+  float* s_epi = reinterpret_cast<float*>(smem + 560);        // [4]
+  int* s_run0 = reinterpret_cast<int*>(smem + 576);           // [4] first head of run n
+  int* s_runlen = reinterpret_cast<int*>(smem + 592);         // [4] heads in run n
+  float* s_red = reinterpret_cast<float*>(smem + 704);        // [64]
+  float4* s_rot4 = reinterpret_cast<float4*>(smem + 4096);    // [32] rotation by 256 positions per frequency pair (cos.xy, sin.xy)
+  float* s_qall = reinterpret_cast<float*>(smem + 1536);      // [4][128]
+  uint8_t* Bsm = smem + kKHeader;
+  uint8_t* Ssm = Bsm + (size_t)p.bsum * 256;
+  int* s_runoff = reinterpret_cast<int*>(smem + 4608);        // [4] byte offset of run n in a tile slot
+  int* s_ring = reinterpret_cast<int*>(smem + 4624);          // [2] tile slots, bytes per tile slot
 
   if (tid == 0) {
-    for (int k = 0; k < kKMaxStages; ++k) {
+    for (int k = 0; k < kKMaxSlots; ++k) {
       mbar_init(st_full + k, 1);
       mbar_init(st_empty + k, 4);
     }
-    for (int k = 0; k < kKASlots; ++k) {
+    for (int k = 0; k < kKAbufs; ++k) {
       mbar_init(a_full + k, 4);
       mbar_init(a_empty + k, 1);
     }
-    for (int k = 0; k < kKAcc; ++k) {
+    for (int k = 0; k < 6 * G; ++k) {
       mbar_init(d_full + k, 1);
-      mbar_init(d_empty + k, 8);
+      mbar_init(d_empty + k, 4);       // the drain warpgroup of the job
     }
-    for (int k = 0; k < kKPart; ++k) mbar_init(p_full + k, 4);
-    for (int k = 0; k < 2; ++k) {
-      mbar_init(w_full + k, 1);
-      mbar_init(w_empty + k, 2);
-    }
-    mbar_init(fin_bar, 2);
+    mbar_init(w_bar, 1);
     *s_abort = 0;
-    s_range[0] = k_unit_start(p, blockIdx.x);
-    s_range[1] = k_unit_start(p, blockIdx.x + 1);
+    int off = 0, nr = 0;
+    for (int g = 0; g < G; ++g) {
+      const int kv = (grp * G + g) / qpk;
+      s_boff[g] = off;
+      s_rank[g] = lay.k_rank[kv];
+      s_src[g] = reinterpret_cast<const uint8_t*>(p.k_cache) + (lay.k_offset[kv] + (int64_t)b * lay.k_batch_stride[kv]) * XB;
+      off += lay.k_rank[kv] * 256;
+      if (g == 0 || kv != (grp * G + g - 1) / qpk) {
+        s_run0[nr] = g;
+        s_runlen[nr] = 0;
+        ++nr;
+      }
+      ++s_runlen[nr - 1];
+    }
+    *s_nruns = nr;
+    mbar_init(fin_bar, nr == G ? 2 : 1);       // one arrival per MMA issuer
+    int tb = 0;
+    for (int n = 0; n < nr; ++n) {
+      s_runoff[n] = tb;
+      tb += 128 * s_rank[s_run0[n]] * XB;
+    }
+    int nt = p.stage_total / tb;
+    if (nt > kKMaxSlots / nr) nt = kKMaxSlots / nr;
+    s_ring[0] = nt;                              // >= 2 (checked on the host)
+    s_ring[1] = tb;
     fence_mbar_init();
-  }
-  if (warp == 2) {                                          // rotation of frequency pair (2i, 2i+1) by 128 positions
-    const int i = lane;
-    float c0, s0, c1, s1;
-    exact_sincos(128, p.inv_freq[2 * i], c0, s0);
-    exact_sincos(128, p.inv_freq[2 * i + 1], c1, s1);
-    s_rot[i] = make_float4(c0, c1, s0, s1);
-    s_w[i] = make_float2(p.inv_freq[2 * i], p.inv_freq[2 * i + 1]);
   }
   if (warp == 0) {
     tmem_alloc(tmem_slot, 512);
@@ -437,353 +474,297 @@ __global__ void __launch_bounds__(kKThreads, 1) k_stream_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int u0 = s_range[0], u1 = s_range[1];
-#ifdef STARKV_KTRACE
-  if (p.trace && tid == 0) {
-    p.trace[kKTraceJobs * kKTraceFields + blockIdx.x * 4 + 0] = (long long)global_timer_ns();
-    p.trace[kKTraceJobs * kKTraceFields + blockIdx.x * 4 + 2] = u1 - u0;
-  }
-#endif
-  const unsigned long long wlim = p.wait_ns;
-  auto fail_at = [&](int code, int line) {
+  const int NR = *s_nruns;
+  const int NT = s_ring[0];                      // tile slots in the ring
+  const int TB = s_ring[1];                      // bytes per tile slot
+  const int U = ntiles * NR;                     // units of this CTA
+
+  auto fail = [&](int code) {
     record_error(p.err, code);
     *s_abort = 1;
-#ifdef STARKV_KTRACE
-    if (p.trace)
-      atomicCAS(reinterpret_cast<unsigned long long*>(p.trace + kKTraceJobs * kKTraceFields + blockIdx.x * 4 + 3), 0ull,
-                (unsigned long long)line);
-#else
-    (void)line;
-#endif
   };
-#define fail(code) fail_at(code, __LINE__)
-  const int NS = p.nstage;
 
   if (wg == 0) {
     regs_dec<kKCtlRegs>();
     if (warp == 0) {
-      // ============================================================ producer
+      // ============================================================ producer warp
+      if (p.wpre && lane == 0) {
+        uint32_t wb = 0;
+        for (int g = 0; g < G; ++g) wb += (uint32_t)s_rank[g] * 256u;
+        mbar_arrive_expect_tx(w_bar, wb);
+        for (int g = 0; g < G; ++g)
+          bulk_g2s(Bsm + s_boff[g], p.wpre + ((int64_t)b * Hq + grp * G + g) * p.wstride, (uint32_t)s_rank[g] * 256u, w_bar);
+      }
+      __syncwarp();
+      int issued = 0;
       if (lane == 0) {
-        KUnitIter it;
-        it.init(u0, u1, p.ntiles, Hkv, G);
-        int i = 0, nseg = 0;
-        for (; it.valid(); it.next(), ++i) {
+        int t = 0, n = 0;                          // tile and run of unit u
+        for (int u = 0; u < U; ++u, issued = u) {
           if (*s_abort) break;
-          const int r = lay.k_rank[it.kv], R = r * XB;
-          if (it.first) {                                   // the segment's W images, job order
-            const int k = it.seg, ws = k % p.nW;
-            nseg = k + 1;
-            if (k >= p.nW && !mbar_wait(w_empty + ws, (uint32_t)(((k / p.nW) & 1) ^ 1), wlim)) { fail(kDevWaitMma); break; }
-            uint32_t wb = 0;
-            for (int gk = 0; gk < G; ++gk) wb += (uint32_t)(qpk * lay.k_rank[it.grp * G + gk] * 256);
-            mbar_arrive_expect_tx(w_full + ws, wb);
-            uint32_t off = 0;
-            for (int gk = 0; gk < G; ++gk) {
-              const int kv = it.grp * G + gk, rk = lay.k_rank[kv];
-              for (int g = 0; g < qpk; ++g) {
-                bulk_g2s(Wsm + (size_t)ws * p.wslot_bytes + off, p.wpre + ((int64_t)it.b * Hq + kv * qpk + g) * p.wstride,
-                         (uint32_t)(rk * 256), w_full + ws);
-                off += (uint32_t)(rk * 256);
-              }
-            }
+          const int ts = t % NT, slot = ts * NR + n;
+          if (!mbar_wait(st_empty + slot, (uint32_t)(((t / NT) & 1) ^ 1), wlim)) { fail(kDevWaitCopy); break; }
+          const int g0 = s_run0[n], R = s_rank[g0] * XB;
+          const int t0 = t_begin + t * 128;
+          const uint32_t bytes = (uint32_t)((tiled ? 128 : min(128, t_end - t0)) * R);
+          const bool skip = u == p.skip_unit && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+          if (!skip) {                               // (test hook: a skipped stage never lands)
+            mbar_arrive_expect_tx(st_full + slot, bytes);
+            bulk_g2s(Ssm + (size_t)ts * TB + s_runoff[n], s_src[g0] + (size_t)t0 * R, bytes, st_full + slot);
           }
-          const int s = i % NS;
-          if (!mbar_wait(st_empty + s, (uint32_t)(((i / NS) & 1) ^ 1), wlim)) { fail(kDevWaitCopy); break; }
-          if (it.u == p.skip_unit) continue;                   // test hook: this stage never lands
-          const int t0 = it.tile * 128;
-          const uint32_t bytes = (uint32_t)((tiled ? 128 : min(128, p.T - t0)) * R);
-          const uint8_t* src = reinterpret_cast<const uint8_t*>(p.k_cache) +
-                               (lay.k_offset[it.kv] + (int64_t)it.b * lay.k_batch_stride[it.kv]) * XB + (int64_t)t0 * R;
-          mbar_arrive_expect_tx(st_full + s, bytes);
-          bulk_g2s(Ssm + (size_t)s * p.stage_bytes, src, bytes, st_full + s);
-          KTRACE(i, 0);
+          if (++n == NR) { n = 0; ++t; }
         }
-        // every copy issued has landed before the CTA may exit (each wait bounded;
-        // a stage that was never issued only costs its time limit)
-        for (int k = max(0, i - NS); k < i; ++k)
-          if (!(u0 + k == p.skip_unit) && !mbar_wait(st_full + k % NS, (uint32_t)((k / NS) & 1), wlim))
-            fail(kDevWaitCopy);
-        for (int k = max(0, nseg - p.nW); k < nseg; ++k)
-          if (!mbar_wait(w_full + k % p.nW, (uint32_t)((k / p.nW) & 1), wlim)) fail(kDevWaitCopy);
+        // every copy issued has landed before the CTA may exit
+        for (int u = max(0, issued - NT * NR); u < issued; ++u) {
+          const int tt = u / NR, slot = (tt % NT) * NR + (u - tt * NR);
+          if (u == p.skip_unit && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) continue;
+          if (!mbar_wait(st_full + slot, (uint32_t)((tt / NT) & 1), wlim)) fail(kDevWaitCopy);   // each bounded
+        }
       }
       __syncwarp();
     } else if (warp == 1 || warp == 2) {
       // ============================================================ MMA issuers
-      // Issuer iw takes the units i with i % 2 == iw (one thread issues a
-      // tcgen05.mma about as fast as the tensor core retires one, so two keep it
-      // busy); both walk every unit to follow the job, A-ring and W offsets.
-      // (With several jobs per unit one issuer keeps the tensor core busy, and
-      // two could run one accumulator phase ahead of the drains.)
+      // When every query head of the group has its own KV head (one job per unit),
+      // warps 1 and 2 issue the units of parity 0 and 1 (the bookkeeping of one
+      // overlaps the MMAs of the other); otherwise warp 1 issues every unit.  Job j
+      // accumulates into accumulator j % 3 and signals job slot j % 6G (the jobs of
+      // one slot share their issuer and their drain warpgroup, so each slot's phases
+      // are waited in order); before reusing accumulator j % 3 the issuer waits for
+      // job j - 3 to be drained (slot (j - 3) % 6G, at most one phase behind: this
+      // issuer waited for job j - 3 - 6G before it issued job j - 6G).
+      named_bar_sync(1, 512 + 96);               // W matrices built (builders + warps 1-3)
+      const int NI = (NR == G) ? 2 : 1;          // issuers
       const int iw = warp - 1;
-      const int NI = qpk == 1 ? 2 : 1;                       // issuers
-      if (lane == 0 && iw < NI) {
+      if (iw < NI && lane == 0) {
+        if (p.wpre && !mbar_wait(w_bar, 0, wlim)) fail(kDevWaitCopy);
         constexpr uint32_t IDESC = idesc_f16_f32(128, 128);
-        KUnitIter it;
-        it.init(u0, u1, p.ntiles, Hkv, G);
-        int j = 0;
-        uint32_t woff = 0;                                  // byte offset of this KV head's W images in the slot
         bool ok = true;
-        for (int i = 0; it.valid() && ok; it.next(), ++i) {
-          if (*s_abort) break;
-          const int r = lay.k_rank[it.kv];
-          const int ws = it.seg % p.nW;
-          const int as = i % nAs;                              // A slot of unit i, used for the (i / nAs)-th time
-          if (it.tfirst) {
-            woff = 0;
-            for (int gk = 0; gk < it.gk; ++gk) woff += (uint32_t)(qpk * lay.k_rank[it.grp * G + gk] * 256);
-          }
-          if (i % NI == iw) {
-            if (it.first && !mbar_wait(w_full + ws, (uint32_t)((it.seg / p.nW) & 1), wlim)) { ok = false; break; }
-            if (!mbar_wait(a_full + as, (uint32_t)((i / nAs) & 1), wlim)) { ok = false; break; }
-            tc_fence_after();
-            KTRACE(j, 4);
-            const uint32_t acol = 384u + (uint32_t)(as * aW);
-            for (int g = 0; g < qpk; ++g) {
-              const int jj = j + g;
-              if (jj >= kKAcc && !mbar_wait(d_empty + jj % kKAcc, (uint32_t)(((jj / kKAcc) - 1) & 1), wlim)) { ok = false; break; }
-              tc_fence_after();
-              KTRACE(jj, 5);
-              const uint64_t bdesc = smem_desc(smem_u32(Wsm + (size_t)ws * p.wslot_bytes + woff + g * r * 256), 128,
-                                               (uint32_t)r * 16u);
-              const uint32_t d = tmem + (uint32_t)(jj % kKAcc) * 128u;
-              for (int kk = 0; kk < (r >> 4); ++kk)
-                mma_f16_ts(d, tmem + acol + 8u * kk, bdesc + (uint64_t)(kk * 16), IDESC, kk ? 1u : 0u);
-              mma_commit(d_full + jj % kKAcc);
-              KTRACE(jj, 6);
+        int t = 0, n = iw;                         // tile and run of unit u
+        if (n >= NR) { n -= NR; ++t; }
+        for (int u = iw; u < U && ok; u += NI) {
+          if (!mbar_wait(a_full + (u & 1), (uint32_t)((u >> 1) & 1), wlim)) { ok = false; break; }
+          const uint32_t a_t = tmem + 384u + (uint32_t)(u & 1) * 64u;
+          const int g0 = s_run0[n], len = s_runlen[n];
+          for (int k = 0; k < len; ++k) {
+            const int g = g0 + k, j = t * G + g;
+            if (j >= kKAcc) {
+              const int jp = j - kKAcc;
+              if (!mbar_wait(d_empty + jp % (6 * G), (uint32_t)((jp / (6 * G)) & 1), wlim)) { ok = false; break; }
             }
-            if (!ok) break;
-            mma_commit(a_empty + as);
+            tc_fence_after();
+            const int r = s_rank[g];
+            const uint64_t bdesc = smem_desc(smem_u32(Bsm + s_boff[g]), 128, (uint32_t)r * 16u);
+            const uint32_t d = tmem + (uint32_t)(j % kKAcc) * 128u;
+            mma_f16_ts(d, a_t, bdesc, IDESC, 0u);
+            for (int kk = 1; kk < (r >> 4); ++kk) mma_f16_ts(d, a_t + kk * 8, bdesc + (uint64_t)(kk * 16), IDESC, 1u);
+            mma_commit(d_full + j % (6 * G));
           }
-          if (it.last_of_seg())                             // every issuer: the slot is free once all retired
-            for (int k = NI; k <= 2; ++k) mma_commit(w_empty + ws);
-          woff += (uint32_t)(qpk * r * 256);
-          j += qpk;
+          mma_commit(a_empty + (u & 1));
+          n += NI;
+          while (n >= NR) { n -= NR; ++t; }
         }
         if (!ok) fail(kDevWaitMma);
         mma_commit(fin_bar);                     // arrives once every MMA of this thread retired
-        if (NI == 1) mma_commit(fin_bar);
         if (!mbar_wait(fin_bar, 0, wlim)) fail(kDevWaitMma);
       }
       __syncwarp();
+    } else {
+      // warp 3: no role after the prologue barrier
+      named_bar_sync(1, 512 + 96);
     }
-  } else if (wg <= 2) {
-    // ============================================================ converter warpgroups
-    // Warpgroup cw takes the units i with i % 2 == cw; both walk every unit to
-    // follow the A ring.
-    regs_dec<kKConvRegs>();
-    const int cw = wg - 1;
-    const int row = tid - 128 * wg;                          // token row = TMEM lane
-    const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-    KUnitIter it;
-    it.init(u0, u1, p.ntiles, Hkv, G);
-    for (int i = 0; it.valid(); it.next(), ++i) {
-      const int r = lay.k_rank[it.kv];
-      const int as = i % nAs;
-      if ((i & 1) == cw) {
+  } else {
+    // ---- build W_g = [P | Q] (fp16, canonical K-major layout) for each head: 512 threads
+    {
+      const int bt = tid - 128;
+      if (p.wpre) {                                    // W came from the pre-pass (bulk-copied by the producer)
+        if (bt < G) s_epi[bt] = p.weta[(int64_t)b * Hq + grp * G + bt] * p.out_scale;
+      } else {
+        for (int e = bt; e < G * 128; e += 512)
+          s_qall[e] = load_as_f32(p.q, p.q_dtype, ((int64_t)b * Hq + grp * G) * 128 + e);
+      }
+      named_bar_sync(2, 512);
+      if (bt >= 64 && bt < 96) {                       // rotation of the pair (2i, 2i + 1) by 256 positions: cos, sin
+        const int i = bt - 64;
+        float c0, s0, c1, s1;
+        exact_sincos(256, p.inv_freq[2 * i], c0, s0);
+        exact_sincos(256, p.inv_freq[2 * i + 1], c1, s1);
+        s_rot4[i] = make_float4(c0, c1, s0, s1);
+      }
+      for (int g = 0; g < G && !p.wpre; ++g) {
+        const int qh = grp * G + g;
+        const float* qv = s_qall + g * 128;
+        float eta;
+        build_w_head<QUANT, 512>(p, b, qh, qv, Bsm + s_boff[g], s_red, bt, [] { named_bar_sync(2, 512); }, eta);
+        if (bt == 0) s_epi[g] = eta * p.out_scale;
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(1, 512 + 96);                       // W ready for the MMA warp (s_epi, s_rot4 for the drains)
+    }
+
+    if (wg <= 2) {
+      // ============================================================ converter warpgroups
+      // Warpgroup c = wg - 1 converts the units u with u % 2 == c into A buffer c.
+      regs_dec<kKConvRegs>();
+      const int cw = wg - 1;
+      const int ct = tid - 128 * wg;                     // token row = TMEM lane
+      const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+      // Each unit is handed to the MMA issuer as soon as its TMEM stores complete
+      // (this warpgroup's next unit waits for the same A buffer to drain).
+      int n = cw, t = 0;                           // run, tile of unit u
+      while (n >= NR) { n -= NR; ++t; }
+      for (int u = cw; u < U; u += 2) {
         if (*s_abort) break;
-        const int s = i % NS;
-        if (!mbar_wait(st_full + s, (uint32_t)((i / NS) & 1), wlim)) { fail(kDevWaitCopy); break; }
-        if (row == 0) KTRACE(i, 1);
-        const int R = r * XB, nch = R >> 4;
-        const int cs = tiled ? 2048 : 16;
-        const uint8_t* srow = Ssm + (size_t)s * p.stage_bytes + (tiled ? row * 16 : row * R);
-        const uint32_t acol = 384u + (uint32_t)(as * aW);
-        // the first piece is converted before the A slots are free (its latency
-        // overlaps the wait), the rest after
-        uint32_t o[32];
-        k_convert_piece<XT, PCH>(srow, cs, min(PCH, nch), o);
-        if (!mbar_wait(a_empty + as, (uint32_t)(((i / nAs) & 1) ^ 1), wlim)) { fail(kDevWaitMma); break; }
-        tc_fence_after();
-        if (row == 0) KTRACE(i, 2);
-        tmem_st_cols(lane_base + acol, o, min(PCH, nch) * CPC);
-        for (int c0 = PCH; c0 < nch; c0 += PCH) {
-          const int n = min(PCH, nch - c0);
-          k_convert_piece<XT, PCH>(srow + c0 * cs, cs, n, o);
-          tmem_st_cols(lane_base + acol + (uint32_t)(c0 * CPC), o, n * CPC);
+        const int g0 = s_run0[n], r = s_rank[g0];
+        const int j = t * G + g0;
+        const int ts = t % NT, s = ts * NR + n;
+        if (!mbar_wait(st_full + s, (uint32_t)((t / NT) & 1), wlim)) { fail(kDevWaitCopy); break; }
+        const int rc = (r * XB) >> 4;
+        const int cs = tiled ? 2048 : 16;            // bytes between a row's 16-byte chunks
+        const uint8_t* srow = Ssm + (size_t)ts * TB + s_runoff[n] + (size_t)ct * (tiled ? 16 : r * XB);
+        const uint32_t taddr = lane_base + 384u + (uint32_t)cw * 64u;
+        auto release = [&] {                       // the stage is read: hand it back to the producer
+          __syncwarp();
+          if (lane == 0) mbar_arrive(st_empty + s);
+        };
+        auto wait_a = [&]() -> bool {              // the A buffer's previous MMAs retired
+          if (!mbar_wait(a_empty + cw, (uint32_t)(((u >> 1) & 1) ^ 1), wlim)) { fail(kDevWaitMma); return false; }
+          tc_fence_after();
+          return true;
+        };
+        bool okc = true;
+        if constexpr (XB == 1) {
+          switch (rc) {
+            case 1: okc = convert_ahead_i8<1>(srow, cs, taddr, release, wait_a); break;
+            case 2: okc = convert_ahead_i8<2>(srow, cs, taddr, release, wait_a); break;
+            case 3: okc = convert_ahead_i8<3>(srow, cs, taddr, release, wait_a); break;
+            case 4: okc = convert_ahead_i8<4>(srow, cs, taddr, release, wait_a); break;
+            case 5: okc = convert_ahead_i8<5>(srow, cs, taddr, release, wait_a); break;
+            case 6: okc = convert_ahead_i8<6>(srow, cs, taddr, release, wait_a); break;
+            default:
+              okc = wait_a();
+              if (okc) convert_row<XT>(rc, srow, cs, taddr);
+              release();
+              break;
+          }
+        } else {
+          okc = wait_a();
+          if (okc) convert_row<XT>(rc, srow, cs, taddr);
+          release();
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(st_empty + s);            // the stage is read: back to the producer
+        if (!okc) break;
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0)
-          mbar_arrive(a_full + as);
-        if (lane == 0) KTRACE(i, (row >> 5) == 0 ? 3 : 12 + (row >> 5));
+        if (lane == 0) mbar_arrive(a_full + cw);
+        n += 2;
+        while (n >= NR) { n -= NR; ++t; }
       }
-    }
-  } else {
-    // ============================================================ drain warpgroups
-    // Half h = wg - 3 takes frequencies [32h, 32h + 32) of every job: cosine
-    // columns [32h, 32h + 32) and sine columns [64 + 32h, 96 + 32h).  The job's
-    // epilogue (sum of the halves, scale, mask, logit, running maximum) is done by
-    // half (j & 1); the other hands its partial sum over in shared memory.
-    regs_inc<kKDrainRegs>();
-    const int h = wg - 3;
-    const int dw = warp & 3;
-    const int row = dw * 32 + lane;
-    const uint32_t lbase = tmem + ((uint32_t)(dw * 32) << 16);
-    float2 cc[16], ss[16];                                   // cos / sin of frequencies (32h + 2i, 32h + 2i + 1)
-    float m_run[8];                                          // running maximum of each job of the segment
-    KUnitIter it;
-    it.init(u0, u1, p.ntiles, Hkv, G);
-    int j = 0;
-    bool ok = true;
-    float madd = 0.f, lpos = 0.f;
-    bool live = false;
-    int l = 0;
-    auto flush_max = [&](int b, int kv0) {                   // the segment's maxima -> per-head global maximum
-      if (!p.smax) return;
+    } else {
+      // ============================================================ drain warpgroups
+      // Warpgroup w = wg - 3 takes every job of the tiles t with t % 2 == w.  Per
+      // job: thread = token row (TMEM lane) with cos / sin of all 64 frequencies at
+      // its token in registers (advanced by 256 positions per tile of its own with
+      // packed fp32x2 rotations), eight 16-column TMEM loads, packed fp32x2 FMAs,
+      // then scale, mask, the logit to HBM and the running maximum per head.
+      regs_inc<kKDrainRegs>();
+      const int w2 = wg - 3;
+      const int dw = warp & 3;                           // TMEM lane quarter
+      const int row = dw * 32 + lane;
+      float2 cs_c[32], cs_s[32];                         // cos / sin of frequencies (2i, 2i+1)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        if (e < GJ) {
-          float m = m_run[e];
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-          if (lane == 0 && m > kNegBig) atomic_max_float(p.smax + (int64_t)b * Hq + kv0 * qpk + e, m);
-        }
-        m_run[e] = kNegBig;
+      for (int i = 0; i < 32; ++i) {
+        exact_sincos(t_begin + 128 * w2 + row, p.inv_freq[2 * i], cs_c[i].x, cs_s[i].x);
+        exact_sincos(t_begin + 128 * w2 + row, p.inv_freq[2 * i + 1], cs_c[i].y, cs_s[i].y);
       }
-    };
+      float m_run[G];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) m_run[e] = kNegBig;
-    int seg_b = it.b, seg_kv0 = it.grp * G;
-    for (; it.valid() && ok; it.next()) {
-      if (*s_abort) break;
-      if (it.first) {
-        if (it.seg > 0) flush_max(seg_b, seg_kv0);
-        seg_b = it.b;
-        seg_kv0 = it.grp * G;
-        named_bar_sync(2 + h, 128);                          // this half's reads of the previous scales are done
-        if (row < GJ) s_esc[h * 8 + row] = p.weta[(int64_t)it.b * Hq + seg_kv0 * qpk + row] * p.out_scale;
-        named_bar_sync(2 + h, 128);
-      }
-      if (it.tfirst) {
-        // ---- RoPE angles of this tile's token rows
-        const int tile = it.tile;
-        int nrot = 1;                                        // rotations by one tile still to apply
-        if (it.first || (tile % kKAnchor) == 0) {
-          const int a = tile - tile % kKAnchor;
-          const int pos = a * 128 + row;
+      for (int g = 0; g < G; ++g) m_run[g] = kNegBig;
+      const uint32_t lbase = tmem + ((uint32_t)(dw * 32) << 16);
+      float* const lg_base = p.logits + ((int64_t)b * Hq + grp * G) * p.T + t_begin + row;
+      bool ok = true;
+      for (int tile = w2; tile < ntiles && ok; tile += 2) {
+        if (*s_abort) { ok = false; break; }
+        if (tile > w2) {                                 // advance every frequency by 256 positions
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float2 w = s_w[16 * h + i];
-            exact_sincos(pos, w.x, cc[i].x, ss[i].x);
-            exact_sincos(pos, w.y, cc[i].y, ss[i].y);
-            asm volatile("" ::: "memory");                   // one frequency pair at a time (register pressure)
+          for (int i = 0; i < 32; ++i) {
+            const float4 r = s_rot4[i];
+            const float2 rc = make_float2(r.x, r.y), rs = make_float2(r.z, r.w);
+            const float2 c = cs_c[i], sn = cs_s[i];
+            const float2 u = __fmul2_rn(sn, rs), v = __fmul2_rn(c, rs);
+            cs_c[i] = __ffma2_rn(c, rc, make_float2(-u.x, -u.y));
+            cs_s[i] = __ffma2_rn(sn, rc, v);
+            asm volatile("" ::: "memory");               // keep each constant's load beside its use (no hoisting)
           }
-          nrot = tile - a;
         }
 #pragma unroll 1
-        for (int k = 0; k < nrot; ++k) {
+        for (int g = 0; g < G; ++g) {
+          const int j = tile * G + g;
+          const int db = j % kKAcc, ds = j % (6 * G);    // accumulator, job slot
+          // the epilogue's operands first, so that their latency overlaps the waits
+          const int l = t_begin + tile * 128 + row;
+          const bool live = l < t_end;
+          const float esc = s_epi[g];
+          const float madd = (p.mask && live) ? p.mask[(int64_t)b * p.T + l] * p.mask_scale : 0.f;
+          float* const dst = lg_base + (int64_t)g * p.T + tile * 128;
+          if (!mbar_wait(d_full + ds, (uint32_t)((j / (6 * G)) & 1), wlim)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t ta = lbase + (uint32_t)db * 128u;
+          float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float4 rt = s_rot[16 * h + i];
-            const float2 rc = make_float2(rt.x, rt.y), rs = make_float2(rt.z, rt.w);
-            const float2 c = cc[i], sn = ss[i];
-            const float2 uu = __fmul2_rn(sn, rs), vv = __fmul2_rn(c, rs);
-            cc[i] = __ffma2_rn(c, rc, make_float2(-uu.x, -uu.y));
-            ss[i] = __ffma2_rn(sn, rc, vv);
-            asm volatile("" ::: "memory");                   // keep each constant's load beside its use
-          }
-        }
-        l = tile * 128 + row;
-        lpos = (float)l;
-        live = l < p.T;
-        madd = (p.mask && live) ? p.mask[(int64_t)it.b * p.T + l] * p.mask_scale : 0.f;
-      }
-#pragma unroll 1
-      for (int g = 0; g < qpk; ++g, ++j) {
-        const int e = it.gk * qpk + g;                       // job within the segment's tile
-        const int acc = j % kKAcc;
-        if (!mbar_wait(d_full + acc, (uint32_t)((j / kKAcc) & 1), wlim)) { ok = false; break; }
-        tc_fence_after();
-        if (row == 0) KTRACE(j, 7 + h);
-        float2 a0 = make_float2(0.f, 0.f), a1 = make_float2(0.f, 0.f);
-        if constexpr (REF) {
-          // The reference's angle is fl(l * w) = l * w - e with e = fma(l, w, -fl(l * w))
-          // exact; cos / sin of it to first order in e (|e| <= half an ulp of the angle):
-          // c + s e and s - c e.
-          const float2 lf = make_float2(lpos, lpos), nlf = make_float2(-lpos, -lpos);
-          {
-            float v[32];
-            tmem_ld32(lbase + (uint32_t)acc * 128u + 32u * h, v);
+          for (int q = 0; q < 8; ++q) {                  // columns [16q, 16q + 16): q < 4 cosine part, else sine part
+            float v[16];
+            tmem_ld16(ta + 16u * q, v);
+            if (q == 7) {                                // accumulator free for the MMA of job j + kKAcc
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(d_empty + ds);
+            }
+            const int f0 = (q & 3) * 8;                  // first frequency pair of this block
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float2 w = s_w[16 * h + i];
-              const float2 er = __ffma2_rn(lf, w, __fmul2_rn(nlf, w));
-              const float2 c = __ffma2_rn(ss[i], er, cc[i]);
-              a0 = __ffma2_rn(c, make_float2(v[2 * i], v[2 * i + 1]), a0);
+            for (int i = 0; i < 8; i += 2) {
+              if (q < 4) {
+                acc0 = __ffma2_rn(cs_c[f0 + i], make_float2(v[2 * i], v[2 * i + 1]), acc0);
+                acc1 = __ffma2_rn(cs_c[f0 + i + 1], make_float2(v[2 * i + 2], v[2 * i + 3]), acc1);
+              } else {
+                acc0 = __ffma2_rn(cs_s[f0 + i], make_float2(v[2 * i], v[2 * i + 1]), acc0);
+                acc1 = __ffma2_rn(cs_s[f0 + i + 1], make_float2(v[2 * i + 2], v[2 * i + 3]), acc1);
+              }
             }
           }
-          {
-            float v[32];
-            tmem_ld32(lbase + (uint32_t)acc * 128u + 64u + 32u * h, v);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty + acc);      // accumulator free for the MMA of job j + 3
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float2 w = s_w[16 * h + i];
-              const float2 ne = __ffma2_rn(nlf, w, __fmul2_rn(lf, w));
-              const float2 sn = __ffma2_rn(cc[i], ne, ss[i]);
-              a1 = __ffma2_rn(sn, make_float2(v[2 * i], v[2 * i + 1]), a1);
-            }
-          }
-        } else {
-          {
-            float v[32];
-            tmem_ld32(lbase + (uint32_t)acc * 128u + 32u * h, v);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) a0 = __ffma2_rn(cc[i], make_float2(v[2 * i], v[2 * i + 1]), a0);
-          }
-          {
-            float v[32];
-            tmem_ld32(lbase + (uint32_t)acc * 128u + 64u + 32u * h, v);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(d_empty + acc);      // accumulator free for the MMA of job j + 3
-#pragma unroll
-            for (int i = 0; i < 16; ++i) a1 = __ffma2_rn(ss[i], make_float2(v[2 * i], v[2 * i + 1]), a1);
-          }
-        }
-        const float part = (a0.x + a0.y) + (a1.x + a1.y);
-        if (row == 0 && h == 0) KTRACE(j, 9);
-        const int ps = j % kKPart;
-        if ((j & 1) != h) {
-          s_part[ps * 128 + row] = part;
-          __syncwarp();
-          if (lane == 0) mbar_arrive(p_full + ps);
-          if (row == 0) KTRACE(j, 10);
-        } else {
-          if (!mbar_wait(p_full + ps, (uint32_t)((j / kKPart) & 1), wlim)) { ok = false; break; }
-          if (row == 0) KTRACE(j, 11);
-          const float val = fmaf(part + s_part[ps * 128 + row], s_esc[h * 8 + e], madd);
+          const float sum = (acc0.x + acc0.y) + (acc1.x + acc1.y);
           if (live) {
-            p.logits[((int64_t)it.b * Hq + it.kv * qpk + g) * p.T + l] = val;
+            const float val = fmaf(sum, esc, madd);
+            *dst = val;
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
-              if (k == e) m_run[k] = fmaxf(m_run[k], val);
+            for (int gg = 0; gg < G; ++gg)
+              if (gg == g) m_run[gg] = fmaxf(m_run[gg], val);
           }
-          if (row == 0) KTRACE(j, 12);
         }
       }
+      if (!ok) fail(kDevWaitMma);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float m = m_run[g];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) s_red[g * 8 + w2 * 4 + dw] = m;
+      }
     }
-    if (ok && !*s_abort) flush_max(seg_b, seg_kv0);
-    if (!ok) fail(kDevWaitMma);
   }
 
-  // ---- teardown (every MMA retired: the issuers waited fin_bar; every copy landed:
-  // the producer waited the last stages)
+  // ---- split statistics and teardown (every MMA retired: the issuer waited fin_bar;
+  // every copy landed: the producer waited the last stages)
   tc_fence_before();
   __syncthreads();
-#ifdef STARKV_KTRACE
-  if (p.trace && tid == 0) p.trace[kKTraceJobs * kKTraceFields + blockIdx.x * 4 + 1] = (long long)global_timer_ns();
-#endif
+  if (p.smax && tid < G && !*s_abort) {
+    float M = s_red[tid * 8];
+#pragma unroll
+    for (int k = 1; k < 8; ++k) M = fmaxf(M, s_red[tid * 8 + k]);
+    p.smax[((int64_t)b * Hq + grp * G + tid) * p.nsplit + split] = M;
+  }
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-#undef fail
 }
 
 }  // namespace starkv

@@ -18,15 +18,10 @@ using namespace starkv;
 namespace {
 
 thread_local char g_last_error[256] = "";
-
 // Test hooks (starkv_set_test_hooks): time limit of one device-side wait and a
 // K-kernel stage whose copy is never issued.
 unsigned long long g_wait_ns = kWaitLimitNs;
 int g_skip_unit = -1;
-#ifdef STARKV_KTRACE
-long long* g_ktrace = nullptr;
-long long* g_vtrace = nullptr;
-#endif
 
 int fail_launch() {
   const cudaError_t e = cudaGetLastError();
@@ -87,53 +82,69 @@ int max_v_rank(const starkv_layout& l) {
 }
 int k_elem_bytes(const starkv_layout& l) { return l.quantized ? 1 : dtype_bytes(l.latent_dtype); }
 
-// K-path geometry: W slots (one (b, kv) segment's qpk W images each) and the
-// staging ring that fit next to them (one CTA per SM: it owns all 512 TMEM columns).
+// K-path geometry: heads per CTA (G) and the shared memory that fits (one CTA
+// per SM: it owns all 512 TMEM columns).
 struct KGeom {
-  int rmax, G, nW, wslot, nstage, stage_bytes;
+  int G, rmax, bsum, stage_total;
   size_t smem;
 };
 
-// Largest group G of KV heads (G * qpk <= 8 jobs per tile share a RoPE rotation)
-// whose W slot(s) leave room for the staging ring.
 KGeom k_geometry(const starkv_layout& l) {
   KGeom g;
-  memset(&g, 0, sizeof(g));
-  const int rmax = max_k_rank(l);
+  g.rmax = max_k_rank(l);
   const int xb = k_elem_bytes(l);
-  const int qpk = l.num_q_heads / l.num_kv_heads;
-  const long avail = (long)kKSmemMax - kKHeader;
-  const long stage = 128L * rmax * xb;
+  const int Hq = l.num_q_heads, qpk = l.num_q_heads / l.num_kv_heads;
+  // Largest G whose W matrices leave room for a staging ring of >= 2 tile slots
+  // (a tile slot: 128 rows of every distinct KV head of the group).
   for (int G = 4; G >= 1; G >>= 1) {
-    if (l.num_kv_heads % G || G * qpk > 8) continue;
-    const long wslot = (long)G * qpk * rmax * 256;
-    for (int nW = 2; nW >= 1; --nW) {
-      long ns = (avail - nW * wslot) / stage;
-      if (ns > kKMaxStages) ns = kKMaxStages;
-      if (ns >= (nW == 2 ? 6 : 4)) {
-        g.rmax = rmax;
-        g.G = G;
-        g.nW = nW;
-        g.wslot = (int)wslot;
-        g.nstage = (int)ns;
-        g.stage_bytes = (int)stage;
-        g.smem = (size_t)kKSmemMax;
-        return g;
+    if (Hq % G) continue;
+    int bsum = 0, tmax = 0;
+    for (int grp = 0; grp < Hq / G; ++grp) {
+      int s = 0, tb = 0;
+      for (int k = 0; k < G; ++k) {
+        const int kv = (grp * G + k) / qpk;
+        s += l.k_rank[kv];
+        if (k == 0 || kv != (grp * G + k - 1) / qpk) tb += 128 * l.k_rank[kv] * xb;
       }
+      bsum = s > bsum ? s : bsum;
+      tmax = tb > tmax ? tb : tmax;
+    }
+    const long st = k_stage_total(bsum);
+    if (st >= 2L * tmax) {
+      g.G = G;
+      g.bsum = bsum;
+      g.stage_total = (int)st;
+      g.smem = (size_t)kKSmemMax;                // one CTA per SM (it owns all 512 TMEM columns)
+      return g;
     }
   }
+  g.G = 0;
+  g.bsum = 0;
+  g.smem = 0;
+  g.rmax = 0;
+  g.stage_total = 0;
   return g;
 }
 
-// Scheduling cost of one unit (128 tokens) of KV head kv: the slowest of its HBM
-// bytes, its tensor-core time (qpk jobs of r/16 MMAs) and its drain time (a
-// fixed TMEM read per job), in SM cycles, plus a fixed hand-off overhead.
-int k_unit_cost(const starkv_layout& l, int kv) {
-  const int r = l.k_rank[kv], qpk = l.num_q_heads / l.num_kv_heads, xb = k_elem_bytes(l);
-  int c = 6 * r * xb;
-  if (4 * qpk * r > c) c = 4 * qpk * r;
-  if (160 * qpk > c) c = 160 * qpk;
-  return c + 64;
+int auto_splits(const starkv_layout& l, int T, int sms) {
+  const KGeom g = k_geometry(l);
+  if (g.G == 0 || T <= 0) return 1;
+  const int ntiles = (T + 127) / 128;
+  const long base = (long)l.batch * (l.num_q_heads / g.G);
+  const long slots = (long)(sms > 0 ? sms : 148);
+  int best = 1;
+  double best_t = 1e30;
+  for (int ns = 1; ns <= ntiles && ns <= 128; ++ns) {
+    const int tiles = (ntiles + ns - 1) / ns;
+    const long ctas = base * ns;
+    const long waves = (ctas + slots - 1) / slots;
+    const double t = (double)waves * (tiles + 1.5);  // ~1.5 tiles of per-CTA fill/prologue
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = ns;
+    }
+  }
+  return best;
 }
 
 // Streaming V kernel (int4 latents, all V blocks per CTA): applicability and shared memory.
@@ -177,36 +188,26 @@ int v2_splits(const starkv_layout& l, int T, int sms) {
   return ns < 1 ? 1 : ns;
 }
 
-// Splits of the per-block V kernel (no streaming kernel for this layout):
-// about two CTAs per SM over (split, block x rank tile, sequence).
-int v1_splits(const starkv_layout& l, int T) {
-  const int ctiles = (max_v_rank(l) + kVCtaRank - 1) / kVCtaRank;
-  const int ntiles = (T + 127) / 128;
-  const long per = (long)l.batch * l.num_v_blocks * ctiles;
-  int ns = (int)((296 + per - 1) / per);
-  if (ns > ntiles) ns = ntiles;
-  return ns < 1 ? 1 : ns;
-}
-
-// Sequence splits of the V pass.
-int v_splits(const starkv_layout& l, int T, int sms) {
-  return v2_geometry(l).ok ? v2_splits(l, T, sms) : v1_splits(l, T);
+// Splits of the V pass: the streaming kernel's own, else the K splits.
+int v_splits(const starkv_layout& l, int T, int ns_k, int sms) {
+  return v2_geometry(l).ok ? v2_splits(l, T, sms) : ns_k;
 }
 
 struct WsLayout {
-  size_t err, logits, smax, lsum, partial, wimg, weta, total;
+  size_t err, logits, stats, partial, wimg, weta, total;
 };
 
-// smax: per-head maximum logit (B, Hq); lsum: V split sums (B, Hq, nsv);
-// partial (B, Hq, nsv, rv_max); W images and their normalisation per (b, head).
-WsLayout ws_layout(const starkv_layout& l, int T, int nsv) {
+// stats: K split maxima (B, Hq, ns_k), then V split sums (B, Hq, nsv); partial (B, Hq, nsv, rv_max).
+// nsv covers both V kernels (the streaming one may fall back at run time).
+WsLayout ws_layout(const starkv_layout& l, int T, int ns_k, int sms) {
   WsLayout w;
   const size_t BH = (size_t)l.batch * l.num_q_heads;
+  const int v2 = v_splits(l, T, ns_k, sms);
+  const size_t nsv = (size_t)(v2 > ns_k ? v2 : ns_k);
   w.err = 0;
   w.logits = 256;
-  w.smax = w.logits + align256(BH * T * sizeof(float));
-  w.lsum = w.smax + align256(BH * sizeof(float));
-  w.partial = w.lsum + align256(BH * nsv * sizeof(float));
+  w.stats = w.logits + align256(BH * T * sizeof(float));
+  w.partial = w.stats + align256(BH * (ns_k + nsv) * sizeof(float));
   w.wimg = w.partial + align256(BH * nsv * max_v_rank(l) * sizeof(float));
   w.weta = w.wimg + align256(BH * (size_t)max_k_rank(l) * 256);
   w.total = w.weta + align256(BH * sizeof(float));
@@ -253,7 +254,7 @@ int validate(const starkv_layout* lp) {
   }
   if (kv != l.num_kv_heads) return set_error(STARKV_ERR_INVALID, "V blocks do not cover the KV heads");
   if (vcol != l.v_rank_total) return set_error(STARKV_ERR_INVALID, "v_rank_total mismatch");
-  if (k_geometry(l).nW == 0) return set_error(STARKV_ERR_UNSUPPORTED, "K ranks x query heads per KV head too large for shared memory (or more than 8)");
+  if (k_geometry(l).G == 0) return set_error(STARKV_ERR_UNSUPPORTED, "K ranks too large for shared memory");
   return STARKV_OK;
 }
 
@@ -271,30 +272,33 @@ inline unsigned grid1d(int64_t n, int threads) {
   return (unsigned)b;
 }
 
-template <typename XT, bool REF>
-int launch_k(const KParams& kp, const KGeom& g, int sms, cudaStream_t st) {
-  auto kern = k_stream_kernel<XT, REF>;
-  const int slot = (sizeof(XT) == 1 ? 0 : sizeof(XT) == 4 ? 1 : std::is_same<XT, __half>::value ? 2 : 3) + (REF ? 4 : 0);
+template <typename XT, bool QUANT, int G>
+int launch_kg(const KParams& kp, const KGeom& g, cudaStream_t st) {
+  auto kern = k_logits_kernel<XT, QUANT, G>;
+  const int slot = 3 * (QUANT ? 0 : (sizeof(XT) == 4 ? 1 : (std::is_same<XT, __half>::value ? 2 : 3))) + (G == 4 ? 0 : G == 2 ? 1 : 2);
   int rc = ensure_smem(kern, g.smem, slot);
   if (rc) return rc;
-  const long long units = (long long)kp.lay.batch * kp.lay.num_kv_heads * kp.ntiles;
-  const int grid = (int)(units < sms ? units : sms);
+  dim3 grid(kp.nsplit, kp.lay.num_q_heads / kp.G, kp.lay.batch);
   kern<<<grid, kKThreads, g.smem, st>>>(kp);
   return fail_launch();
 }
 
-template <bool REF>
-int dispatch_k_ref(const KParams& kp, const KGeom& g, int sms, cudaStream_t st) {
-  if (kp.lay.quantized) return launch_k<int8_t, REF>(kp, g, sms, st);
-  switch (kp.lay.latent_dtype) {
-    case STARKV_F16: return launch_k<__half, REF>(kp, g, sms, st);
-    case STARKV_BF16: return launch_k<__nv_bfloat16, REF>(kp, g, sms, st);
-    default: return launch_k<float, REF>(kp, g, sms, st);
+template <typename XT, bool QUANT>
+int launch_k(const KParams& kp, const KGeom& g, cudaStream_t st) {
+  switch (kp.G) {
+    case 4: return launch_kg<XT, QUANT, 4>(kp, g, st);
+    case 2: return launch_kg<XT, QUANT, 2>(kp, g, st);
+    default: return launch_kg<XT, QUANT, 1>(kp, g, st);
   }
 }
 
-int dispatch_k(const KParams& kp, const KGeom& g, int sms, cudaStream_t st) {
-  return kp.ref_angles ? dispatch_k_ref<true>(kp, g, sms, st) : dispatch_k_ref<false>(kp, g, sms, st);
+int dispatch_k(const KParams& kp, const KGeom& g, cudaStream_t st) {
+  if (kp.lay.quantized) return launch_k<int8_t, true>(kp, g, st);
+  switch (kp.lay.latent_dtype) {
+    case STARKV_F16: return launch_k<__half, false>(kp, g, st);
+    case STARKV_BF16: return launch_k<__nv_bfloat16, false>(kp, g, st);
+    default: return launch_k<float, false>(kp, g, st);
+  }
 }
 
 template <typename LT, bool QUANT>
@@ -339,12 +343,8 @@ int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp
     return set_error(STARKV_ERR_INVALID, "k_cache must be 16-byte aligned");
   if (a->num_tokens <= 0 || a->num_tokens > lay->capacity)
     return set_error(STARKV_ERR_INVALID, "num_tokens outside (0, capacity]");
-  if (!a->workspace) return set_error(STARKV_ERR_INVALID, "null workspace");
-  if (reinterpret_cast<uintptr_t>(a->workspace) % 256) return set_error(STARKV_ERR_INVALID, "workspace not 256-byte aligned");
   rc = check_device();
   if (rc) return rc;
-  if ((long long)lay->batch * lay->num_kv_heads * ((a->num_tokens + 127) / 128) > 0x7fffffffLL)
-    return set_error(STARKV_ERR_UNSUPPORTED, "batch x KV heads x tiles exceeds 2^31 units");
   g = k_geometry(*lay);
   memset(&kp, 0, sizeof(kp));
   kp.lay = *lay;
@@ -355,45 +355,14 @@ int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp
   kp.q_dtype = a->q_dtype;
   kp.w_dtype = a->w_dtype;
   kp.T = a->num_tokens;
-  kp.ntiles = (a->num_tokens + 127) / 128;
-  kp.nW = g.nW;
   kp.G = g.G;
   kp.rmax = g.rmax;
-  kp.wslot_bytes = g.wslot;
-  kp.nstage = g.nstage;
-  kp.stage_bytes = g.stage_bytes;
+  kp.bsum = g.bsum;
+  kp.stage_total = g.stage_total;
   kp.inv_freq = a->inv_freq;
-  kp.wstride = g.rmax * 256;
-  long long cs = 0;
-  for (int h = 0; h < lay->num_kv_heads; ++h) {
-    kp.cost[h] = k_unit_cost(*lay, h);
-    cs += (long long)kp.cost[h] * kp.ntiles;
-  }
-  kp.cost_seq = cs;
   kp.wait_ns = g_wait_ns;
   kp.skip_unit = g_skip_unit;
-  // The reference rounds each RoPE angle to fp32; once angles reach 2^16 rad that
-  // rounding (up to 2^-8 rad) shows in the outputs, so the kernel reproduces it.
-  kp.ref_angles = (double)(a->num_tokens - 1) >= 65536.0 ? 1 : 0;
-#ifdef STARKV_KTRACE
-  kp.trace = g_ktrace;
-#endif
   return STARKV_OK;
-}
-
-// The K path: W pre-pass (+ maximum reset), then the persistent K kernel.
-int run_k(KParams& kp, const KGeom& g, uint8_t* ws, const WsLayout& w, cudaStream_t st) {
-  kp.wpre = ws + w.wimg;
-  kp.weta = reinterpret_cast<float*>(ws + w.weta);
-  kp.err = reinterpret_cast<int*>(ws + w.err);
-  const dim3 wgrid(kp.lay.num_q_heads, kp.lay.batch);
-  if (kp.lay.quantized)
-    k_wprep_kernel<true><<<wgrid, 256, 0, st>>>(kp, ws + w.wimg, reinterpret_cast<float*>(ws + w.weta));
-  else
-    k_wprep_kernel<false><<<wgrid, 256, 0, st>>>(kp, ws + w.wimg, reinterpret_cast<float*>(ws + w.weta));
-  int rc = fail_launch();
-  if (rc) return rc;
-  return dispatch_k(kp, g, device_sm_count(nullptr), st);
 }
 
 template <typename LT, bool QUANT>
@@ -425,7 +394,7 @@ const char* starkv_last_error(void) { return g_last_error; }
 int32_t starkv_auto_splits(const starkv_layout* lay, int32_t num_tokens) {
   if (validate(lay)) return 1;
   const int sms = device_sm_count(nullptr);
-  return v_splits(*lay, num_tokens, sms > 0 ? sms : 148);
+  return auto_splits(*lay, num_tokens, sms > 0 ? sms : 148);
 }
 
 int starkv_project_append(const starkv_layout* lay, const void* hidden, int32_t hidden_size, const void* vs_k,
@@ -464,7 +433,8 @@ int starkv_decode_workspace_size(const starkv_layout* lay, int32_t num_tokens, i
   if (rc) return rc;
   if (!bytes || num_tokens <= 0) return set_error(STARKV_ERR_INVALID, "bad arguments");
   const int ns = num_splits > 0 ? num_splits : starkv_auto_splits(lay, num_tokens);
-  *bytes = ws_layout(*lay, num_tokens, ns).total;
+  const int sms = device_sm_count(nullptr);
+  *bytes = ws_layout(*lay, num_tokens, ns, sms > 0 ? sms : 148).total;
   return STARKV_OK;
 }
 
@@ -560,35 +530,56 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   KGeom g;
   int rc = prepare_k(lay, a, kp, g);
   if (rc) return rc;
-  if (!a->v_cache || !a->v_u || !a->out) return set_error(STARKV_ERR_INVALID, "null argument");
+  if (!a->v_cache || !a->v_u || !a->out || !a->workspace) return set_error(STARKV_ERR_INVALID, "null argument");
   if (lay->quantized && !a->v_params) return set_error(STARKV_ERR_INVALID, "quantised layout needs v_params");
-  if (lay->quantized &&
-      (reinterpret_cast<uintptr_t>(a->v_cache) % 16 || reinterpret_cast<uintptr_t>(a->v_params) % 16))
-    return set_error(STARKV_ERR_INVALID, "v_cache and v_params must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(a->workspace) % 256) return set_error(STARKV_ERR_INVALID, "workspace not 256-byte aligned");
   const int T = a->num_tokens;
   const int sms = device_sm_count(nullptr);
-  const int nsv = a->num_splits > 0 ? a->num_splits : v_splits(*lay, T, sms);
-  const WsLayout w = ws_layout(*lay, T, nsv);
+  const int ns = a->num_splits > 0 ? a->num_splits : auto_splits(*lay, T, sms);
+  const WsLayout w = ws_layout(*lay, T, ns, sms);
   if (a->workspace_bytes < w.total) return set_error(STARKV_ERR_WORKSPACE, "workspace too small");
   cudaStream_t st = (cudaStream_t)stream;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
 
+  const int ntiles = (T + 127) / 128;
+  const int tiles_per = (ntiles + ns - 1) / ns;
   kp.mask = a->mask;
   kp.logits = reinterpret_cast<float*>(ws + w.logits);
-  kp.smax = reinterpret_cast<float*>(ws + w.smax);
+  // W of every (sequence, query head) once, ahead of the K kernel (its CTAs bulk-copy theirs)
+  kp.wstride = max_k_rank(*lay) * 256;
+  kp.wpre = ws + w.wimg;
+  kp.weta = reinterpret_cast<float*>(ws + w.weta);
+  kp.smax = reinterpret_cast<float*>(ws + w.stats);     // split maxima, then split sums (same region)
+  kp.err = reinterpret_cast<int*>(ws + w.err);
+  kp.nsplit = ns;
+  kp.tps = tiles_per * 128;
   const float log2e = 1.4426950408889634f;
   kp.out_scale = a->scaling * log2e;
   kp.mask_scale = log2e;
   cudaEvent_t const* ev = reinterpret_cast<cudaEvent_t const*>(a->events);
   if (ev) cudaEventRecord(ev[0], st);
-  rc = run_k(kp, g, ws, w, st);
+  {
+    const dim3 wg(lay->num_q_heads, lay->batch);
+    if (lay->quantized)
+      k_wprep_kernel<true><<<wg, 256, 0, st>>>(kp, ws + w.wimg, reinterpret_cast<float*>(ws + w.weta));
+    else
+      k_wprep_kernel<false><<<wg, 256, 0, st>>>(kp, ws + w.wimg, reinterpret_cast<float*>(ws + w.weta));
+    rc = fail_launch();
+    if (rc) return rc;
+  }
+  rc = dispatch_k(kp, g, st);
   if (rc) return rc;
   if (ev) cudaEventRecord(ev[1], st);
 
+  if (lay->quantized &&
+      (reinterpret_cast<uintptr_t>(a->v_cache) % 16 || reinterpret_cast<uintptr_t>(a->v_params) % 16))
+    return set_error(STARKV_ERR_INVALID, "v_cache and v_params must be 16-byte aligned");
   const V2Geom vg = v2_geometry(*lay);
-  float* lsum = reinterpret_cast<float*>(ws + w.lsum);
+  const bool stream_v = vg.ok;
+  const int nsv = stream_v ? v2_splits(*lay, T, sms) : ns;
+  float* lsum = kp.smax + (size_t)lay->batch * lay->num_q_heads * ns;
   float* partial = reinterpret_cast<float*>(ws + w.partial);
-  if (vg.ok) {
+  if (stream_v) {
     V2Params v2;
     memset(&v2, 0, sizeof(v2));
     v2.lay = *lay;
@@ -601,15 +592,12 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
     v2.err = kp.err;
     v2.T = T;
     v2.nsplit = nsv;
-    v2.nsplit_k = 1;
+    v2.nsplit_k = ns;
     v2.tps = ((T + nsv * kV2Tile - 1) / (nsv * kV2Tile)) * kV2Tile;
     v2.rv_max = max_v_rank(*lay);
     v2.nstages = vg.nstages;
     v2.stage_bytes = vg.stage_bytes;
     v2.b_bytes = vg.b_bytes;
-#ifdef STARKV_KTRACE
-    v2.trace = g_vtrace;
-#endif
     rc = vg.np == 16 ? launch_v2<16>(v2, vg, st) : launch_v2<32>(v2, vg, st);
   } else {
     VParams vp;
@@ -622,12 +610,12 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
     vp.v_params = reinterpret_cast<const __half2*>(a->v_params);
     vp.partial = partial;
     vp.T = T;
-    vp.nsplit = nsv;
-    vp.nsplit_k = 1;
-    vp.tps = ((kp.ntiles + nsv - 1) / nsv) * 128;
+    vp.nsplit = ns;
+    vp.nsplit_k = ns;
+    vp.tps = kp.tps;
     vp.rv_max = max_v_rank(*lay);
     vp.err = kp.err;
-    rc = dispatch_v(vp, nsv, st);
+    rc = dispatch_v(vp, ns, st);
   }
   if (rc) return rc;
   if (ev) cudaEventRecord(ev[2], st);
@@ -655,12 +643,15 @@ int starkv_k_logits(const starkv_layout* lay, const starkv_decode_args* a, float
   int rc = prepare_k(lay, a, kp, g);
   if (rc) return rc;
   if (!logits) return set_error(STARKV_ERR_INVALID, "logits is required");
-  const WsLayout w = ws_layout(*lay, a->num_tokens, 1);
-  if (a->workspace_bytes < w.total) return set_error(STARKV_ERR_WORKSPACE, "workspace too small");
+  const int T = a->num_tokens;
+  const int ns = a->num_splits > 0 ? a->num_splits : auto_splits(*lay, T, device_sm_count(nullptr));
+  const int ntiles = (T + 127) / 128;
   kp.logits = logits;
+  kp.nsplit = ns;
+  kp.tps = ((ntiles + ns - 1) / ns) * 128;
   kp.out_scale = 1.0f;
   kp.mask_scale = 1.0f;
-  return run_k(kp, g, reinterpret_cast<uint8_t*>(a->workspace), w, (cudaStream_t)stream);
+  return dispatch_k(kp, g, (cudaStream_t)stream);
 }
 
 int starkv_v_latent(const starkv_layout* lay, const float* probs, int32_t num_tokens, const void* v_cache,
@@ -689,18 +680,6 @@ int starkv_v_latent(const starkv_layout* lay, const float* probs, int32_t num_to
   vp.rv_max = max_v_rank(*lay);
   return dispatch_v(vp, 1, st);
 }
-
-#ifdef STARKV_KTRACE
-// Diagnostic builds only (not declared in starkv.h): K-kernel timeline buffer.
-int starkv_debug_ktrace(void* buf) {
-  g_ktrace = reinterpret_cast<long long*>(buf);
-  return STARKV_OK;
-}
-int starkv_debug_vtrace(void* buf) {
-  g_vtrace = reinterpret_cast<long long*>(buf);
-  return STARKV_OK;
-}
-#endif
 
 int starkv_quantize_split(const void* x, int32_t dtype, int64_t rows, int32_t r, int32_t split_r, void* up_q,
                           void* s_up, void* lo_q, void* s_lo, starkv_stream_t stream) {
@@ -805,8 +784,8 @@ int starkv_decode_attention_static(const starkv_layout* lay, const starkv_decode
     return set_error(STARKV_ERR_INVALID, "num_tokens outside (0, capacity]");
   const int sms = device_sm_count(nullptr);
   if (sms < 0) return set_error(STARKV_ERR_LAUNCH, "no CUDA device");
-  const int ns = args->num_splits > 0 ? args->num_splits : v_splits(*lay, args->num_tokens, sms);
-  const size_t need = ws_layout(*lay, args->num_tokens, ns).total;
+  const int ns = args->num_splits > 0 ? args->num_splits : auto_splits(*lay, args->num_tokens, sms);
+  const size_t need = ws_layout(*lay, args->num_tokens, ns, sms).total;
   if (need > kStaticScratchBytes) {
     char msg[200];
     snprintf(msg, sizeof(msg),
