@@ -167,7 +167,7 @@ def workload_config(spec, n):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="c1")
@@ -346,7 +346,8 @@ def main():
     roofline = {"kernel": "k_logits_kernel<int8_t,true,G> (fused K reconstruction + RoPE + q.k, split maxima)",
                 "bound": "hbm", "achieved": k_gbs, "peak": peak, "unit": "GB/s", "frac": k_gbs / peak,
                 "peak_kind": peak_kind,
-                "traffic": (traffic or {}).get("dram_bytes_per_launch_full_size"),
+                # the committed ncu capture is of the full 1-GPU workload: per-rank traffic at N > 1 is not measured
+                "traffic": (traffic or {}).get("dram_bytes_per_launch_full_size") if world == 1 else None,
                 "algorithmic_bytes_per_launch": k_bytes, "avg_launch_ms": k_ms}
     line = {
         "metric": METRIC, "value": spec.batch / (ms / 1e3), "unit": UNIT, "n_gpus": world,

@@ -15,7 +15,8 @@
 // TMEM drain.  The query is folded into W once per CTA, so neither the keys
 // nor the rotated keys are ever materialised.
 //
-// CTA = (sequence split, group of G query heads, sequence b), 640 threads, one
+// CTA = (sequence b, group of G query heads, split of the group's tokens; each
+// group has its own split count, chosen on the host to balance ragged ranks), 640 threads, one
 // CTA per SM (it owns the 512 TMEM columns).  A "unit" is one 128-token tile of
 // one KV head (the G heads form runs of heads that share a KV head); a "job" is
 // one (tile, query head) pair.  Roles, handing off through mbarriers (every wait
@@ -52,6 +53,8 @@
 
 namespace starkv {
 
+constexpr int kKMaxGroups = 64;  // head groups per layer (Hq / G)
+
 struct KParams {
   starkv_layout lay;
   const void* q;
@@ -64,7 +67,9 @@ struct KParams {
   float* smax;            // (B, Hq, nsplit) maximum logit of each split, or null
   int* err;
   int q_dtype, w_dtype;
-  int T, nsplit, tps;     // tokens, splits, tokens per split (multiple of 128)
+  int T, nsplit, tps;     // tokens, split stride of smax (the most splits of any group), unused
+  int ngroups, splits_seq;                   // head groups; CTAs per sequence (sum of gsplit)
+  int gsplit[kKMaxGroups];                   // sequence splits of each head group
   int G, rmax, bsum;      // heads per CTA, max rank, max per-group rank sum (W matrices in smem)
   int stage_total;        // bytes of the staging ring
   float out_scale;        // multiplier of q.k (scaling * log2 e for decode)
@@ -73,7 +78,7 @@ struct KParams {
   const float* weta;      //   then the CTA builds its W itself; eta of every (sequence, query head)
   int wstride;            // bytes per (sequence, query head) W image
   unsigned long long wait_ns;  // time limit of one device wait
-  int skip_unit;          // test hook: CTA (0, 0, 0) never issues this unit's copy (-1: off)
+  int skip_unit;          // test hook: the first CTA never issues this unit's copy (-1: off)
 };
 
 constexpr int kKThreads = 640;
@@ -380,6 +385,8 @@ __global__ void __launch_bounds__(256) k_wprep_kernel(const __grid_constant__ KP
   float eta;
   build_w_head<QUANT, 256>(p, b, qh, qv, wout + ((int64_t)b * Hq + qh) * p.wstride, red, t, [] { __syncthreads(); }, eta);
   if (t == 0) eout[(int64_t)b * Hq + qh] = eta;
+  if (p.smax)                                      // splits a group does not use stay at "minus infinity"
+    for (int k = t; k < p.nsplit; k += 256) p.smax[((int64_t)b * Hq + qh) * p.nsplit + k] = kNegBig;
 }
 
 template <typename XT, bool QUANT, int G>
@@ -387,11 +394,17 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int wg = __shfl_sync(0xffffffffu, warp >> 2, 0);   // warpgroup 0..4 (warp-uniform)
-  const int split = blockIdx.x, grp = blockIdx.y, b = blockIdx.z;
+  // CTA = (sequence b, head group, split of that group); groups have their own
+  // split counts (cost-balanced on the host), CTAs are numbered b-major.
+  const int b = blockIdx.x / p.splits_seq;
+  int grp = 0, split = blockIdx.x - b * p.splits_seq;
+  while (split >= p.gsplit[grp]) split -= p.gsplit[grp++];
+  const int gns = p.gsplit[grp];
+  const int gtps = (((p.T + 127) / 128 + gns - 1) / gns) * 128;
   const starkv_layout& lay = p.lay;
   const int Hq = lay.num_q_heads, qpk = Hq / lay.num_kv_heads;
-  const int t_begin = split * p.tps;
-  const int t_end = min(p.T, t_begin + p.tps);
+  const int t_begin = split * gtps;
+  const int t_end = min(p.T, t_begin + gtps);
   const int ntiles = t_end > t_begin ? (t_end - t_begin + 127) / 128 : 0;
   constexpr int XB = (int)sizeof(XT);
   const bool tiled = lay.k_tiled != 0;                   // tiles stored as 16-byte column chunks (starkv.h)
@@ -506,7 +519,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
           const int g0 = s_run0[n], R = s_rank[g0] * XB;
           const int t0 = t_begin + t * 128;
           const uint32_t bytes = (uint32_t)((tiled ? 128 : min(128, t_end - t0)) * R);
-          const bool skip = u == p.skip_unit && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
+          const bool skip = u == p.skip_unit && blockIdx.x == 0;
           if (!skip) {                               // (test hook: a skipped stage never lands)
             mbar_arrive_expect_tx(st_full + slot, bytes);
             bulk_g2s(Ssm + (size_t)ts * TB + s_runoff[n], s_src[g0] + (size_t)t0 * R, bytes, st_full + slot);
@@ -516,7 +529,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         // every copy issued has landed before the CTA may exit
         for (int u = max(0, issued - NT * NR); u < issued; ++u) {
           const int tt = u / NR, slot = (tt % NT) * NR + (u - tt * NR);
-          if (u == p.skip_unit && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) continue;
+          if (u == p.skip_unit && blockIdx.x == 0) continue;
           if (!mbar_wait(st_full + slot, (uint32_t)((tt / NT) & 1), wlim)) fail(kDevWaitCopy);   // each bounded
         }
       }

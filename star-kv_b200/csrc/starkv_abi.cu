@@ -126,25 +126,85 @@ KGeom k_geometry(const starkv_layout& l) {
   return g;
 }
 
-int auto_splits(const starkv_layout& l, int T, int sms) {
+// Sequence splits of each head group for the K kernel (the cost-ordered
+// scheduler of the grouped K path): a group's tile costs the slowest of its HBM
+// bytes, its tensor-core instructions and its drain work, so groups of high
+// ranks get more splits; the split counts are chosen so that all CTAs carry
+// about the same work and fill whole waves of SMs.  override > 0: every group
+// gets that many splits.
+struct KSplits {
+  int ns_max, S, ngroups;
+  int gs[kKMaxGroups];
+};
+
+KSplits k_splits(const starkv_layout& l, int T, int sms, int override_ns) {
+  KSplits r;
+  memset(&r, 0, sizeof(r));
   const KGeom g = k_geometry(l);
-  if (g.G == 0 || T <= 0) return 1;
-  const int ntiles = (T + 127) / 128;
-  const long base = (long)l.batch * (l.num_q_heads / g.G);
-  const long slots = (long)(sms > 0 ? sms : 148);
-  int best = 1;
-  double best_t = 1e30;
-  for (int ns = 1; ns <= ntiles && ns <= 128; ++ns) {
-    const int tiles = (ntiles + ns - 1) / ns;
-    const long ctas = base * ns;
+  const int G = g.G > 0 ? g.G : 1;
+  const int ntiles = T > 0 ? (T + 127) / 128 : 1;
+  const int ng = l.num_q_heads / G;
+  r.ngroups = ng;
+  if (override_ns > 0 || ng > kKMaxGroups) {
+    const int ns = override_ns > 0 ? override_ns : 1;
+    for (int k = 0; k < ng && k < kKMaxGroups; ++k) r.gs[k] = ns;
+    r.ns_max = ns;
+    r.S = ns * ng;
+    return r;
+  }
+  const int xb = k_elem_bytes(l), qpk = l.num_q_heads / l.num_kv_heads;
+  double cost[kKMaxGroups];
+  for (int grp = 0; grp < ng; ++grp) {
+    double bytes = 0, mma = 0;
+    for (int k = 0; k < G; ++k) {
+      const int qh = grp * G + k, kv = qh / qpk;
+      if (k == 0 || kv != (qh - 1) / qpk) bytes += 128.0 * l.k_rank[kv] * xb;
+      mma += (l.k_rank[kv] / 16) * 70.0;           // cycles per tcgen05.mma with two issuers
+    }
+    const double hbm = bytes / 22.0;                 // cycles at one SM's share of HBM bandwidth
+    const double drain = 320.0 * G;                  // cycles of the two drain warpgroups per job
+    double c = hbm > mma ? hbm : mma;
+    c = c > drain ? c : drain;
+    cost[grp] = c + 100.0;
+  }
+  const long slots = sms > 0 ? sms : 148;
+  double best = 1e300;
+  for (int base = 1; base <= 64; ++base) {         // splits of the cheapest-per-tile reference group
+    double cmin = 1e300;
+    for (int grp = 0; grp < ng; ++grp) cmin = cost[grp] < cmin ? cost[grp] : cmin;
+    const double W = cmin * ntiles / base;           // target work per CTA
+    int gs[kKMaxGroups], S = 0, nsm = 0;
+    double worst = 0;
+    for (int grp = 0; grp < ng; ++grp) {
+      int ns = (int)ceil(cost[grp] * ntiles / W - 1e-9);
+      ns = ns < 1 ? 1 : (ns > ntiles ? ntiles : ns);
+      ns = ns > 64 ? 64 : ns;
+      gs[grp] = ns;
+      S += ns;
+      nsm = ns > nsm ? ns : nsm;
+      const double work = cost[grp] * (((ntiles + ns - 1) / ns) + 3.0);   // + per-CTA fill / prologue
+      worst = work > worst ? work : worst;
+    }
+    const long ctas = (long)l.batch * S;
     const long waves = (ctas + slots - 1) / slots;
-    const double t = (double)waves * (tiles + 1.5);  // ~1.5 tiles of per-CTA fill/prologue
-    if (t < best_t - 1e-9) {
-      best_t = t;
-      best = ns;
+    if (waves > 2 && base > 1) continue;            // many small CTAs lose more to their prologues than they gain
+    const double t = (double)waves * worst;
+    if (t < best - 1e-9) {
+      best = t;
+      r.S = S;
+      r.ns_max = nsm;
+      for (int grp = 0; grp < ng; ++grp) r.gs[grp] = gs[grp];
     }
   }
-  return best;
+  return r;
+}
+
+int auto_splits(const starkv_layout& l, int T, int sms) { return k_splits(l, T, sms, 0).ns_max; }
+
+void set_k_splits(KParams& kp, const KSplits& ks) {
+  kp.ngroups = ks.ngroups;
+  kp.splits_seq = ks.S;
+  for (int k = 0; k < kKMaxGroups; ++k) kp.gsplit[k] = ks.gs[k];
 }
 
 // Streaming V kernel (int4 latents, all V blocks per CTA): applicability and shared memory.
@@ -278,7 +338,7 @@ int launch_kg(const KParams& kp, const KGeom& g, cudaStream_t st) {
   const int slot = 3 * (QUANT ? 0 : (sizeof(XT) == 4 ? 1 : (std::is_same<XT, __half>::value ? 2 : 3))) + (G == 4 ? 0 : G == 2 ? 1 : 2);
   int rc = ensure_smem(kern, g.smem, slot);
   if (rc) return rc;
-  dim3 grid(kp.nsplit, kp.lay.num_q_heads / kp.G, kp.lay.batch);
+  dim3 grid(kp.lay.batch * kp.splits_seq);
   kern<<<grid, kKThreads, g.smem, st>>>(kp);
   return fail_launch();
 }
@@ -535,11 +595,13 @@ int starkv_decode_attention(const starkv_layout* lay, const starkv_decode_args* 
   if (reinterpret_cast<uintptr_t>(a->workspace) % 256) return set_error(STARKV_ERR_INVALID, "workspace not 256-byte aligned");
   const int T = a->num_tokens;
   const int sms = device_sm_count(nullptr);
-  const int ns = a->num_splits > 0 ? a->num_splits : auto_splits(*lay, T, sms);
+  const KSplits ks = k_splits(*lay, T, sms, a->num_splits);
+  const int ns = ks.ns_max;
   const WsLayout w = ws_layout(*lay, T, ns, sms);
   if (a->workspace_bytes < w.total) return set_error(STARKV_ERR_WORKSPACE, "workspace too small");
   cudaStream_t st = (cudaStream_t)stream;
   uint8_t* ws = reinterpret_cast<uint8_t*>(a->workspace);
+  set_k_splits(kp, ks);
 
   const int ntiles = (T + 127) / 128;
   const int tiles_per = (ntiles + ns - 1) / ns;
@@ -644,8 +706,10 @@ int starkv_k_logits(const starkv_layout* lay, const starkv_decode_args* a, float
   if (rc) return rc;
   if (!logits) return set_error(STARKV_ERR_INVALID, "logits is required");
   const int T = a->num_tokens;
-  const int ns = a->num_splits > 0 ? a->num_splits : auto_splits(*lay, T, device_sm_count(nullptr));
+  const KSplits ks = k_splits(*lay, T, device_sm_count(nullptr), a->num_splits);
+  const int ns = ks.ns_max;
   const int ntiles = (T + 127) / 128;
+  set_k_splits(kp, ks);
   kp.logits = logits;
   kp.nsplit = ns;
   kp.tps = ((ntiles + ns - 1) / ns) * 128;
@@ -802,7 +866,6 @@ int starkv_decode_attention_static(const starkv_layout* lay, const starkv_decode
   starkv_decode_args a = *args;
   a.workspace = scratch;
   a.workspace_bytes = kStaticScratchBytes;
-  a.num_splits = ns;
   return starkv_decode_attention(lay, &a, stream);
 }
 

@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
   uint64_t* st_full = bars;            // [4]
   uint64_t* st_empty = bars + 4;       // [4]  12 dequant warps
   uint64_t* a_full = bars + 8;         // [6]  the slot's dequant warp pair
-  uint64_t* a_empty = bars + 14;       // [6]  commit
+  uint64_t* a_empty = bars + 14;       // [6]  commit of the pair's MMAs
   uint64_t* b_full = bars + 20;        // [2]  2 prob warps
   uint64_t* b_empty = bars + 22;       // [2]  commit
   uint64_t* fin_bar = bars + 24;
@@ -585,11 +585,12 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       mbar_init(a_full + k, 2);        // the slot's warp pair
       mbar_init(a_empty + k, 1);
     }
+    const int npairs = min((R + 127) / 128, kV2Abufs);     // dequant pairs that issue MMAs
     for (int k = 0; k < 2; ++k) {
       mbar_init(b_full + k, 2);
-      mbar_init(b_empty + k, 1);
+      mbar_init(b_empty + k, npairs);
     }
-    mbar_init(fin_bar, 1);
+    mbar_init(fin_bar, npairs);
     *s_abort = 0;
     for (int j = 0; j < lay.num_v_blocks; ++j)
       for (int c = lay.v_col[j]; c < lay.v_col[j] + lay.v_rank[j]; c += 32) s_cblk[c >> 5] = (uint8_t)j;
@@ -650,37 +651,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ============================================================ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t IDESC = (1u << 4) | (1u << 15) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-      int mc = 0;
-      bool ok = true;
-      for (int t = 0; t < ntiles && ok; ++t) {
-        if (*s_abort) break;
-        const int tb = t & 1;
-        if (!mbar_wait(b_full + tb, (uint32_t)((t >> 1) & 1))) { ok = false; break; }
-        VTRACE(t, 3);
-        const uint32_t bt = smem_u32(Bsm + tb * p.b_bytes);
-        for (int m = 0; m < MU; ++m, ++mc) {
-          const int k = mc % kV2Abufs;
-          if (!mbar_wait(a_full + k, (uint32_t)((mc / kV2Abufs) & 1))) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t ad = smem_desc(smem_u32(Asm + k * kV2ABytes), 128, 1024);
-          const uint64_t bd = smem_desc(bt, 128, 1024);
-          const uint32_t d = tmem + (uint32_t)(m * NP);
-#pragma unroll
-          for (int ks = 0; ks < kV2Tile / 16; ++ks)
-            mma_f16_ss(d, ad + (uint64_t)(ks * 16), bd + (uint64_t)(ks * 16), IDESC, (t > 0 || ks > 0) ? 1u : 0u);
-          mma_commit(a_empty + k);
-        }
-        mma_commit(b_empty + tb);
-        VTRACE(t, 4);
-      }
-      if (!ok) fail(kDevWaitMma);
-      mma_commit(fin_bar);
-      if (!mbar_wait(fin_bar, 0)) fail(kDevWaitMma);
-    }
-    __syncwarp();
+    // (warp 1 has no role: the dequant warp pairs issue their own units' MMAs)
   } else if (warp < 4) {
     // ============================================================ prob warps
     const int pw = warp - 2, pt = tid - 64;
@@ -691,11 +662,12 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
     }
     named_bar_sync(1, 64);
     const int G8 = (Hq + 7) >> 3;                  // groups of 8 heads (the last may be partial)
+    constexpr int QG = NP / 8;                     // head groups a B tile holds
     // destination of this lane's (head, 8-token block) in a B tile, per head group
-    int dstoff[kV2MaxHeads / 8];
-    float mh[kV2MaxHeads / 8], psum[kV2MaxHeads / 8];
+    int dstoff[QG];
+    float mh[QG], psum[QG];
 #pragma unroll
-    for (int q = 0; q < kV2MaxHeads / 8; ++q) {
+    for (int q = 0; q < QG; ++q) {
       dstoff[q] = 0;
       mh[q] = 0.f;
       psum[q] = 0.f;
@@ -706,10 +678,10 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       }
     }
     const int kb = (lane >> 3) + 4 * pw;           // 8-token block of the tile
-    auto load_lg = [&](int t, float (&lg)[kV2MaxHeads / 8][8]) {
+    auto load_lg = [&](int t, float (&lg)[QG][8]) {
       const int l0 = t_begin + t * kV2Tile + kb * 8;
 #pragma unroll
-      for (int q = 0; q < kV2MaxHeads / 8; ++q)
+      for (int q = 0; q < QG; ++q)
         if (q < G8) {
           const float* src = p.logits + ((int64_t)b * Hq + q * 8 + (lane & 7)) * p.T + l0;
 #pragma unroll
@@ -717,17 +689,19 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
             lg[q][e] = (q * 8 + (lane & 7) < Hq && t < ntiles && l0 + e < t_end) ? __ldg(src + e) : kNegBig;
         }
     };
-    float lg[kV2MaxHeads / 8][8];
+    // the next tile's logits are loaded while this tile's weights are formed
+    float lg[QG][8], lgn[QG][8];
+    load_lg(0, lg);
     bool ok = true;
     for (int t = 0; t < ntiles; ++t) {
       if (*s_abort) break;
       const int tb = t & 1;
       const int l0 = t_begin + t * kV2Tile + kb * 8;
-      load_lg(t, lg);
+      load_lg(t + 1, lgn);
       if (!mbar_wait(b_empty + tb, (uint32_t)(((t >> 1) & 1) ^ 1))) { ok = false; break; }
       uint8_t* Bt = Bsm + tb * p.b_bytes + kb * 128;
 #pragma unroll
-      for (int q = 0; q < kV2MaxHeads / 8; ++q)
+      for (int q = 0; q < QG; ++q)
         if (q < G8) {
           __align__(16) __half hv[8];
 #pragma unroll
@@ -742,11 +716,15 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       __syncwarp();
       if (lane == 0) mbar_arrive(b_full + tb);
       if (tid == 64) VTRACE(t, 2);
+#pragma unroll
+      for (int q = 0; q < QG; ++q)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) lg[q][e] = lgn[q][e];
     }
     if (!ok) fail(kDevWaitMma);
     // sum over the 4 lanes of a head (same lane & 7), then over the two warps
 #pragma unroll
-    for (int q = 0; q < kV2MaxHeads / 8; ++q) {
+    for (int q = 0; q < QG; ++q) {
       float v = psum[q];
       v += __shfl_xor_sync(0xffffffffu, v, 8);
       v += __shfl_xor_sync(0xffffffffu, v, 16);
@@ -757,15 +735,20 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       for (int h = pt; h < Hq; h += 64) p.lsum[((int64_t)b * Hq + h) * p.nsplit + split] = s_ps[h] + s_ps[64 + h];
   } else {
     // ============================================================ dequant warps
-    // Six warp pairs: pair p fills A slot p with the M units whose running
-    // index mc = t * MU + m is p mod 6, so six M units are in flight.
+    // Six warp pairs: pair p owns A slot p and the M units m with m % 6 == p.
+    // Per tile it dequantises each of its units into its slot and lane 0 of its
+    // first warp issues that unit's MMAs (one thread waits about as long per
+    // tcgen05.mma as the tensor core takes for one, so several issuing pairs keep
+    // it busy); a unit's accumulator therefore always grows in tile order.
     const int dw = warp - 4;                       // 0..11
     const int pair = dw >> 1, pl = (dw & 1) * 32 + lane;
-    int mc = 0;
+    const bool issuer = (dw & 1) == 0 && lane == 0;
+    constexpr uint32_t IDESC = (1u << 4) | (1u << 15) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    int uc = 0;                                    // units this pair processed
     bool ok = true;
     for (int t = 0; t < ntiles && ok; ++t) {
       if (*s_abort) break;
-      const int s = t % NS;
+      const int s = t % NS, tb = t & 1;
       if (!mbar_wait(st_full + s, (uint32_t)((t / NS) & 1))) { ok = false; break; }
       if (dw == 0 && lane == 0) VTRACE(t, 1);
       const uint8_t* codes = Ssm + (size_t)s * p.stage_bytes;
@@ -777,10 +760,10 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       const int64_t pend = v2_param_end(pstart + (int64_t)nrows * par_row, ptotal);
       const int pcopied = pend > (pstart & ~(int64_t)15) ? (int)(pend - (pstart & ~(int64_t)15)) : 0;
       const uint8_t* gpars = p.v_params + pstart;
-      for (int m = 0; m < MU; ++m, ++mc) {
-        const int k = mc % kV2Abufs;
-        if (k != pair) continue;
-        if (!mbar_wait(a_empty + k, (uint32_t)(((mc / kV2Abufs) & 1) ^ 1))) { ok = false; break; }
+      bool have_b = false;
+      for (int m = pair; m < MU && ok; m += kV2Abufs, ++uc) {
+        const int k = pair;
+        if (!mbar_wait(a_empty + k, (uint32_t)((uc & 1) ^ 1))) { ok = false; break; }
         const int c0 = m * 128;                              // first global channel of the M unit
         const int nch = min(128, R - c0);
         const int gc = nch >> 5;                             // 32-channel groups in the M tile
@@ -794,11 +777,31 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(a_full + k);
+        if (issuer) {
+          bool good = mbar_wait(a_full + k, (uint32_t)(uc & 1));   // both warps of the pair wrote the slot
+          if (good && !have_b) good = mbar_wait(b_full + tb, (uint32_t)((t >> 1) & 1));
+          if (!good) {
+            fail(kDevWaitMma);
+          } else {
+            have_b = true;
+            tc_fence_after();
+            const uint64_t ad = smem_desc(smem_u32(A), 128, 1024);
+            const uint64_t bd = smem_desc(smem_u32(Bsm + tb * p.b_bytes), 128, 1024);
+            const uint32_t d = tmem + (uint32_t)(m * NP);
+#pragma unroll
+            for (int ks = 0; ks < kV2Tile / 16; ++ks)
+              mma_f16_ss(d, ad + (uint64_t)(ks * 16), bd + (uint64_t)(ks * 16), IDESC, (t > 0 || ks > 0) ? 1u : 0u);
+            mma_commit(a_empty + k);
+          }
+        }
+        __syncwarp();
       }
+      if (issuer && pair < MU) mma_commit(b_empty + tb);    // this pair's reads of the tile's B are queued
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(st_empty + s);
       if (dw == 0 && lane == 0) VTRACE(t, 5);
     }
+    if (issuer && pair < MU) mma_commit(fin_bar);          // arrives once this pair's MMAs retired
     if (!ok) fail(kDevWaitMma);
     // ---- epilogue: accumulators -> split partials (warp quarter = TMEM lanes)
     const bool have = ntiles > 0 && !*s_abort;

@@ -147,11 +147,14 @@ def run_case(name, ref_dir):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("STARKV_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("STARKV_REFERENCE"),
+                    help="checkout of the reference (or set STARKV_REFERENCE)")
     ap.add_argument("--only", nargs="*")
     args = ap.parse_args()
     manifest = {}
     for name in (args.only or CASES):
+        if not args.ref:
+            ap.error("pass --ref or set STARKV_REFERENCE to the reference checkout")
         spec, res = run_case(name, args.ref)
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **res)

@@ -58,3 +58,30 @@ def test_project_append_matches_append(cuda, cfg, over, H):
         want = (hidden.float().reshape(L.batch, H) @ vs.float().T).to(dt).float().cpu().numpy()
         got = lat.float().reshape(L.batch, -1).cpu().numpy()
         assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 1e-3
+
+
+@pytest.mark.parametrize("batch", [4, 12])
+def test_step_from_hidden_routes_by_batch(cuda, batch):
+    """``DecodeLayer.step_from_hidden`` uses the fused projection up to 8 sequences and
+    two cuBLAS GEMMs + ``starkv_append`` above; both give the attention of
+    ``append(hidden @ VS^T)`` (the latents may differ in the last bit: GEMM
+    accumulation order), within the decode tolerance."""
+    spec = make_spec("c1", seed=22, num_q_heads=8, batch=batch, context=300)
+    st = build_step(make_layer(spec), cuda)
+    L = st.layer
+    H = 512
+    g = torch.Generator(device=cuda).manual_seed(5)
+    dt = L.cache.latent_dtype
+    hidden = torch.randn(batch, 1, H, generator=g, device=cuda).to(dt)
+    vs_k = (torch.randn(L.layout.k_rank_total, H, generator=g, device=cuda) / H ** 0.5).to(dt)
+    vs_v = (torch.randn(L.layout.v_rank_total, H, generator=g, device=cuda) / H ** 0.5).to(dt)
+    ref_cache = _clone(L.cache)
+    out = torch.empty(batch, spec.num_q_heads, 128, dtype=torch.float32, device=cuda)
+    L.step_from_hidden(st.q, hidden, vs_k, vs_v, out=out)
+    k_lat = (hidden.float() @ vs_k.float().T).to(dt)
+    v_lat = (hidden.float() @ vs_v.float().T).to(dt)
+    ref_cache.append(k_lat.contiguous(), v_lat.contiguous())
+    want = ops.decode_attention(L.layout, ref_cache, st.q, L.k_u, L.v_u, L.inv_freq, L.scaling,
+                                ref_cache.length).float().cpu().numpy()
+    got = out.cpu().numpy()
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 2e-3
