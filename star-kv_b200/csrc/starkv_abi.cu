@@ -126,6 +126,29 @@ KGeom k_geometry(const starkv_layout& l) {
   return g;
 }
 
+// One split count for every head group: the fewest waves of CTAs times the
+// tiles per CTA (plus ~1.5 tiles of fill / prologue per CTA).
+int uniform_splits(const starkv_layout& l, int T, int sms) {
+  const KGeom g = k_geometry(l);
+  if (g.G == 0 || T <= 0) return 1;
+  const int ntiles = (T + 127) / 128;
+  const long base = (long)l.batch * (l.num_q_heads / g.G);
+  const long slots = (long)(sms > 0 ? sms : 148);
+  int best = 1;
+  double best_t = 1e30;
+  for (int ns = 1; ns <= ntiles && ns <= 128; ++ns) {
+    const int tiles = (ntiles + ns - 1) / ns;
+    const long ctas = base * ns;
+    const long waves = (ctas + slots - 1) / slots;
+    const double t = (double)waves * (tiles + 1.5);
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = ns;
+    }
+  }
+  return best;
+}
+
 // Sequence splits of each head group for the K kernel (the cost-ordered
 // scheduler of the grouped K path): a group's tile costs the slowest of its HBM
 // bytes, its tensor-core instructions and its drain work, so groups of high
@@ -168,6 +191,18 @@ KSplits k_splits(const starkv_layout& l, int T, int sms, int override_ns) {
     cost[grp] = c + 100.0;
   }
   const long slots = sms > 0 ? sms : 148;
+  // start from one split per group (one wave when it fits), then let heavier
+  // groups take the SMs that are left
+  r.S = ng;
+  r.ns_max = 1;
+  for (int grp = 0; grp < ng; ++grp) r.gs[grp] = 1;
+  if ((long)l.batch * ng > slots) {               // more than one wave already: the uniform split search
+    const int ns = uniform_splits(l, T, sms);
+    for (int grp = 0; grp < ng; ++grp) r.gs[grp] = ns;
+    r.S = ns * ng;
+    r.ns_max = ns;
+    return r;
+  }
   double best = 1e300;
   for (int base = 1; base <= 64; ++base) {         // splits of the cheapest-per-tile reference group
     double cmin = 1e300;
@@ -187,7 +222,7 @@ KSplits k_splits(const starkv_layout& l, int T, int sms, int override_ns) {
     }
     const long ctas = (long)l.batch * S;
     const long waves = (ctas + slots - 1) / slots;
-    if (waves > 2 && base > 1) continue;            // many small CTAs lose more to their prologues than they gain
+    if (waves > 1) continue;                         // measured: a second wave of CTAs costs more than it balances
     const double t = (double)waves * worst;
     if (t < best - 1e-9) {
       best = t;
