@@ -627,7 +627,6 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
       for (int u = cw; u < U; u += 2) {
         if (*s_abort) break;
         const int g0 = s_run0[n], r = s_rank[g0];
-        const int j = t * G + g0;
         const int ts = t % NT, s = ts * NR + n;
         if (!mbar_wait(st_full + s, (uint32_t)((t / NT) & 1), wlim)) { fail(kDevWaitCopy); break; }
         const int rc = (r * XB) >> 4;

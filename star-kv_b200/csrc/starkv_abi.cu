@@ -149,12 +149,12 @@ int uniform_splits(const starkv_layout& l, int T, int sms) {
   return best;
 }
 
-// Sequence splits of each head group for the K kernel (the cost-ordered
-// scheduler of the grouped K path): a group's tile costs the slowest of its HBM
-// bytes, its tensor-core instructions and its drain work, so groups of high
-// ranks get more splits; the split counts are chosen so that all CTAs carry
-// about the same work and fill whole waves of SMs.  override > 0: every group
-// gets that many splits.
+// Sequence splits of each head group for the K kernel.  The kernel takes a
+// split count per head group (so that groups of high ranks could take more
+// CTAs); on B200 a cost-balanced choice (the slowest of HBM bytes, tensor
+// instructions and drain work per group) measured slower than one uniform
+// count (c1: 0.58-0.80 ms against 0.555 ms), so every group gets
+// uniform_splits.  override > 0: every group gets that many splits.
 struct KSplits {
   int ns_max, S, ngroups;
   int gs[kKMaxGroups];
@@ -165,72 +165,12 @@ KSplits k_splits(const starkv_layout& l, int T, int sms, int override_ns) {
   memset(&r, 0, sizeof(r));
   const KGeom g = k_geometry(l);
   const int G = g.G > 0 ? g.G : 1;
-  const int ntiles = T > 0 ? (T + 127) / 128 : 1;
   const int ng = l.num_q_heads / G;
+  const int ns = override_ns > 0 ? override_ns : uniform_splits(l, T, sms);
   r.ngroups = ng;
-  if (override_ns > 0 || ng > kKMaxGroups) {
-    const int ns = override_ns > 0 ? override_ns : 1;
-    for (int k = 0; k < ng && k < kKMaxGroups; ++k) r.gs[k] = ns;
-    r.ns_max = ns;
-    r.S = ns * ng;
-    return r;
-  }
-  const int xb = k_elem_bytes(l), qpk = l.num_q_heads / l.num_kv_heads;
-  double cost[kKMaxGroups];
-  for (int grp = 0; grp < ng; ++grp) {
-    double bytes = 0, mma = 0;
-    for (int k = 0; k < G; ++k) {
-      const int qh = grp * G + k, kv = qh / qpk;
-      if (k == 0 || kv != (qh - 1) / qpk) bytes += 128.0 * l.k_rank[kv] * xb;
-      mma += (l.k_rank[kv] / 16) * 70.0;           // cycles per tcgen05.mma with two issuers
-    }
-    const double hbm = bytes / 22.0;                 // cycles at one SM's share of HBM bandwidth
-    const double drain = 320.0 * G;                  // cycles of the two drain warpgroups per job
-    double c = hbm > mma ? hbm : mma;
-    c = c > drain ? c : drain;
-    cost[grp] = c + 100.0;
-  }
-  const long slots = sms > 0 ? sms : 148;
-  // start from one split per group (one wave when it fits), then let heavier
-  // groups take the SMs that are left
-  r.S = ng;
-  r.ns_max = 1;
-  for (int grp = 0; grp < ng; ++grp) r.gs[grp] = 1;
-  if ((long)l.batch * ng > slots) {               // more than one wave already: the uniform split search
-    const int ns = uniform_splits(l, T, sms);
-    for (int grp = 0; grp < ng; ++grp) r.gs[grp] = ns;
-    r.S = ns * ng;
-    r.ns_max = ns;
-    return r;
-  }
-  double best = 1e300;
-  for (int base = 1; base <= 64; ++base) {         // splits of the cheapest-per-tile reference group
-    double cmin = 1e300;
-    for (int grp = 0; grp < ng; ++grp) cmin = cost[grp] < cmin ? cost[grp] : cmin;
-    const double W = cmin * ntiles / base;           // target work per CTA
-    int gs[kKMaxGroups], S = 0, nsm = 0;
-    double worst = 0;
-    for (int grp = 0; grp < ng; ++grp) {
-      int ns = (int)ceil(cost[grp] * ntiles / W - 1e-9);
-      ns = ns < 1 ? 1 : (ns > ntiles ? ntiles : ns);
-      ns = ns > 64 ? 64 : ns;
-      gs[grp] = ns;
-      S += ns;
-      nsm = ns > nsm ? ns : nsm;
-      const double work = cost[grp] * (((ntiles + ns - 1) / ns) + 3.0);   // + per-CTA fill / prologue
-      worst = work > worst ? work : worst;
-    }
-    const long ctas = (long)l.batch * S;
-    const long waves = (ctas + slots - 1) / slots;
-    if (waves > 1) continue;                         // measured: a second wave of CTAs costs more than it balances
-    const double t = (double)waves * worst;
-    if (t < best - 1e-9) {
-      best = t;
-      r.S = S;
-      r.ns_max = nsm;
-      for (int grp = 0; grp < ng; ++grp) r.gs[grp] = gs[grp];
-    }
-  }
+  for (int k = 0; k < ng && k < kKMaxGroups; ++k) r.gs[k] = ns;
+  r.ns_max = ns;
+  r.S = ns * ng;
   return r;
 }
 
@@ -350,6 +290,7 @@ int validate(const starkv_layout* lp) {
   if (kv != l.num_kv_heads) return set_error(STARKV_ERR_INVALID, "V blocks do not cover the KV heads");
   if (vcol != l.v_rank_total) return set_error(STARKV_ERR_INVALID, "v_rank_total mismatch");
   if (k_geometry(l).G == 0) return set_error(STARKV_ERR_UNSUPPORTED, "K ranks too large for shared memory");
+  if (l.num_q_heads / k_geometry(l).G > kKMaxGroups) return set_error(STARKV_ERR_UNSUPPORTED, "more than 64 K head groups");
   return STARKV_OK;
 }
 
