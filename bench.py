@@ -290,6 +290,7 @@ def main():
             step(kev[i])
         t1.record()
         torch.cuda.synchronize()
+    assert ops.read_device_error(device=dev) == 0, "a device wait timed out in the timed region"
     if world > 1:
         dist.barrier()
     ms = t0.elapsed_time(t1) / K
@@ -360,8 +361,14 @@ def main():
             if torch.equal(got, ref):
                 check = "bit-exact"
             else:
-                d = (got.float() - ref.float()).abs().max().item()
-                check = f"MISMATCH max_abs={d:.3e}"
+                # shards accumulate V tiles in a different grouping when a shard has
+                # fewer than six 128-channel units (per-replica accumulators), so the
+                # outputs may differ in the last bits: the north-star tolerance applies
+                g, r = got.float(), ref.float()
+                d = (g - r).abs().max().item()
+                rel = ((g - r).norm() / r.norm()).item()
+                ok = rel <= 2e-3 and d <= 1e-2
+                check = f"{'within-tolerance' if ok else 'MISMATCH'} rel_l2={rel:.2e} max_abs={d:.2e}"
         dist.barrier()
 
     if rank != 0:

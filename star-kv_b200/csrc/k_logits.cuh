@@ -85,6 +85,8 @@ constexpr int kKThreads = 640;
 // Register budget per warpgroup after setmaxnreg: control, two converters, two
 // drains (32 + 2*64 + 2*160 = 480 <= 5 * 96, the launch budget).
 constexpr int kKCtlRegs = 32, kKConvRegs = 64, kKDrainRegs = 160;
+static_assert(kKCtlRegs + 2 * kKConvRegs + 2 * kKDrainRegs <= 5 * (65536 / kKThreads / 8 * 8),
+              "setmaxnreg split above the registers the CTA is launched with");
 constexpr int kKAbufs = 2;       // A buffers in TMEM (columns [384, 512)), one per converter warpgroup
 constexpr int kKAcc = 3;         // accumulators in TMEM (columns [0, 384))
 constexpr int kKHeader = 12288;  // barriers / scratch / partial-logit ring at the start of dynamic smem

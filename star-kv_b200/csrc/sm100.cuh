@@ -86,28 +86,16 @@ __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete.  Returns false
-// (and leaves the barrier alone) when limit_ns passes first.  try_wait with a
-// suspend-time hint puts the waiting warp to sleep in hardware until the phase
-// completes (or the hint runs out), so waiting warps take no issue slots from
-// working ones; the timer is checked between such sleeps.
-__device__ __forceinline__ bool mbar_try_wait_for(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
-      : "memory");
-  return ok != 0;
-}
-
+// (and leaves the barrier alone) when limit_ns passes first.  Each try_wait
+// blocks for the hardware's own time limit (no suspend-time hint: a hint of a
+// few microseconds measured 2-3 % slower on the decode kernels, the woken warps
+// resuming later); the timer is checked between the attempts.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           unsigned long long limit_ns = kWaitLimitNs) {
-  if (mbar_try_wait_for(bar, parity, 20000u)) return true;
+  if (mbar_try_wait_plain(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
 #pragma unroll 1
-  while (!mbar_try_wait_for(bar, parity, 20000u))
+  while (!mbar_try_wait_plain(bar, parity))
     if (global_timer_ns() - t0 > limit_ns) return false;
   return true;
 }

@@ -203,12 +203,12 @@ V2Geom v2_geometry(const starkv_layout& l) {
   if (Hq > 32 || units > kV2MaxUnits || units * g.np > 512) return g;
   g.stage_bytes = v2_stage_bytes(R);
   g.b_bytes = g.np * 128;
-  const long fixed = (long)kV2Header + (long)kV2Abufs * kV2ABytes + 2L * g.b_bytes;
+  const long fixed = (long)kV2Header + (long)kV2Abufs * kV2ABytes + (long)v2_bbufs(R) * g.b_bytes;
   long ns = (227L * 1024 - fixed) / g.stage_bytes;
   if (ns > kV2MaxStages) ns = kV2MaxStages;
   if (ns < 2) return g;
   g.nstages = (int)ns;
-  g.smem = v2_smem_bytes(g.nstages, g.stage_bytes, g.b_bytes);
+  g.smem = v2_smem_bytes(g.nstages, g.stage_bytes, g.b_bytes, v2_bbufs(R));
   if (g.smem < 116 * 1024) g.smem = 116 * 1024;                 // one CTA per SM (512 TMEM columns)
   g.ok = true;
   return g;

@@ -416,12 +416,17 @@ __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ Co
 //   dequant warps (12, six pairs): per "M unit" = 128 consecutive channels of the
 //                   whole latent row, q*s + z (one fp16 rounding, channels in the
 //                   order [0,4,1,5,2,6,3,7] within every 8) into one of 6 MN-major
-//                   A tiles (128 channels x 64 tokens); pair p owns A tile p;
+//                   A tiles (128 channels x 64 tokens); lane 0 of a pair's first
+//                   warp issues the unit's 4 tcgen05.mma (M=128, N=NP >= Hq,
+//                   K=16) into the unit's accumulator D[channel, head] in TMEM.
+//                   With U >= 6 units pair p takes the units p, p + 6, ... of every
+//                   tile; with U < 6 (a head shard) each unit gets floor(6 / U)
+//                   pairs, replica j taking the tiles t = j mod replicas into its
+//                   own accumulator, summed in the epilogue;
 //   prob warps (2): p = exp2(logit - M_h) for every head (M_h = maximum over the
-//                   K splits), fp16(p * 2^12) into one K-major B tile of all heads
-//                   (double-buffered by tile), and the running sum of p;
-//   MMA thread:     4 tcgen05.mma (M=128, N=NP >= Hq, K=16) per M unit and tile
-//                   into the unit's accumulator D[channel, head] in TMEM.
+//                   K splits), fp16(p * 2^12) into a K-major B tile of all heads
+//                   (two per replica, tile t in buffer t mod 2 * replicas), and the
+//                   running sum of p.
 // At the end the dequant warps read the accumulators and write the split
 // partials of each channel's own V block heads; the prob warps write the split
 // sums of p.  The combine kernel divides by the total sum.
@@ -460,6 +465,18 @@ struct V2Params {
 #endif
 
 
+// Dequant warp pairs per tile and accumulator replicas: with U = ceil(R / 128) M
+// units, U >= 6 keeps all six pairs on every tile (pair p takes units p, p + 6, ...);
+// U < 6 gives each unit floor(6 / U) pairs, replica j taking the tiles t with
+// t % replicas == j into its own accumulator (summed at the end), so a layer
+// with few V channels (a head shard) still dequantises with most warps.
+__host__ __device__ inline int v2_tile_pairs(int R) { const int u = (R + 127) / 128; return u < 6 ? u : 6; }
+__host__ __device__ inline int v2_replicas(int R) { const int u = (R + 127) / 128; return u < 6 ? 6 / u : 1; }
+// B tiles (probabilities): two per replica, tile t in buffer t % (2 * replicas), so
+// the previous use of a pair's buffer was that same pair's tile (no pair can run
+// a barrier phase ahead of the prob warps).
+__host__ __device__ inline int v2_bbufs(int R) { return 2 * v2_replicas(R); }
+
 __host__ __device__ inline int v2_stage_bytes(int R) {
   return ((kV2Tile * (R / 2) + kV2Tile * (R / 8) + 32) + 127) & ~127;
 }
@@ -470,8 +487,8 @@ __host__ __device__ inline int64_t v2_param_end(int64_t end, int64_t total) {
   const int64_t up = (end + 15) & ~(int64_t)15;
   return up <= total ? up : (end & ~(int64_t)15);
 }
-__host__ __device__ inline size_t v2_smem_bytes(int nstages, int stage_bytes, int b_bytes) {
-  return (size_t)kV2Header + (size_t)nstages * stage_bytes + (size_t)kV2Abufs * kV2ABytes + 2 * (size_t)b_bytes;
+__host__ __device__ inline size_t v2_smem_bytes(int nstages, int stage_bytes, int b_bytes, int nbb) {
+  return (size_t)kV2Header + (size_t)nstages * stage_bytes + (size_t)kV2Abufs * kV2ABytes + (size_t)nbb * b_bytes;
 }
 
 // 32 int4 codes (16 bytes, even channel in the low nibble) -> 4 x 8 fp16 of q*s + z
@@ -555,17 +572,18 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
   const int t_begin = split * p.tps, t_end = min(p.T, t_begin + p.tps);
   const int ntiles = t_end > t_begin ? (t_end - t_begin + kV2Tile - 1) / kV2Tile : 0;
   const int NS = p.nstages;
+  const int NB = v2_bbufs(lay.v_rank_total);      // B tiles
   const int code_row = R / 2, par_row = R / 8;
   const int64_t ptotal = (int64_t)lay.batch * lay.capacity * par_row;   // bytes of the parameter buffer
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 1536);
   uint64_t* st_full = bars;            // [4]
-  uint64_t* st_empty = bars + 4;       // [4]  12 dequant warps
+  uint64_t* st_empty = bars + 4;       // [4]  the active dequant warps
   uint64_t* a_full = bars + 8;         // [6]  the slot's dequant warp pair
   uint64_t* a_empty = bars + 14;       // [6]  commit of the pair's MMAs
-  uint64_t* b_full = bars + 20;        // [2]  2 prob warps
-  uint64_t* b_empty = bars + 22;       // [2]  commit
-  uint64_t* fin_bar = bars + 24;
+  uint64_t* b_full = bars + 20;        // [NB <= 12]  2 prob warps
+  uint64_t* b_empty = bars + 32;       // [NB]  commits of the tile's pairs
+  uint64_t* fin_bar = bars + 44;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 192);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 196);
   int* s_nunits = reinterpret_cast<int*>(smem + 200);
@@ -579,18 +597,17 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
   if (tid == 0) {
     for (int k = 0; k < kV2MaxStages; ++k) {
       mbar_init(st_full + k, 1);
-      mbar_init(st_empty + k, 12);
+      mbar_init(st_empty + k, 2 * v2_tile_pairs(R) * v2_replicas(R));
     }
     for (int k = 0; k < kV2Abufs; ++k) {
       mbar_init(a_full + k, 2);        // the slot's warp pair
       mbar_init(a_empty + k, 1);
     }
-    const int npairs = min((R + 127) / 128, kV2Abufs);     // dequant pairs that issue MMAs
-    for (int k = 0; k < 2; ++k) {
+    for (int k = 0; k < v2_bbufs(R); ++k) {
       mbar_init(b_full + k, 2);
-      mbar_init(b_empty + k, npairs);
+      mbar_init(b_empty + k, v2_tile_pairs(R));
     }
-    mbar_init(fin_bar, npairs);
+    mbar_init(fin_bar, v2_tile_pairs(R) * v2_replicas(R));
     *s_abort = 0;
     for (int j = 0; j < lay.num_v_blocks; ++j)
       for (int c = lay.v_col[j]; c < lay.v_col[j] + lay.v_rank[j]; c += 32) s_cblk[c >> 5] = (uint8_t)j;
@@ -598,7 +615,7 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
     fence_mbar_init();
   }
   // zero the B tiles once: padded heads stay zero
-  for (int e = tid; e < (2 * p.b_bytes) / 16; e += kV2Threads) reinterpret_cast<uint4*>(Bsm)[e] = make_uint4(0u, 0u, 0u, 0u);
+  for (int e = tid; e < (v2_bbufs(R) * p.b_bytes) / 16; e += kV2Threads) reinterpret_cast<uint4*>(Bsm)[e] = make_uint4(0u, 0u, 0u, 0u);
   if (warp == 0) {                     // one CTA per SM: all 512 columns
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
@@ -693,12 +710,14 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
     float lg[QG][8], lgn[QG][8];
     load_lg(0, lg);
     bool ok = true;
+    int tb = 0;                                    // B tile t % NB
+    uint32_t bph = 0;                              // parity of its (t / NB)-th use
     for (int t = 0; t < ntiles; ++t) {
+      if (t > 0 && ++tb == NB) { tb = 0; bph ^= 1; }
       if (*s_abort) break;
-      const int tb = t & 1;
       const int l0 = t_begin + t * kV2Tile + kb * 8;
       load_lg(t + 1, lgn);
-      if (!mbar_wait(b_empty + tb, (uint32_t)(((t >> 1) & 1) ^ 1))) { ok = false; break; }
+      if (!mbar_wait(b_empty + tb, bph ^ 1)) { ok = false; break; }
       uint8_t* Bt = Bsm + tb * p.b_bytes + kb * 128;
 #pragma unroll
       for (int q = 0; q < QG; ++q)
@@ -735,21 +754,42 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       for (int h = pt; h < Hq; h += 64) p.lsum[((int64_t)b * Hq + h) * p.nsplit + split] = s_ps[h] + s_ps[64 + h];
   } else {
     // ============================================================ dequant warps
-    // Six warp pairs: pair p owns A slot p and the M units m with m % 6 == p.
-    // Per tile it dequantises each of its units into its slot and lane 0 of its
-    // first warp issues that unit's MMAs (one thread waits about as long per
-    // tcgen05.mma as the tensor core takes for one, so several issuing pairs keep
-    // it busy); a unit's accumulator therefore always grows in tile order.
+    // Warp pair p (p < TP * RF active pairs, TP = pairs per tile, RF = replicas)
+    // takes the units m = p % TP, m + 6, ... of the tiles t with t % RF == p / TP,
+    // into A slots p, p + TP * RF, ... (a pair keeps several tiles in flight when
+    // fewer than six pairs work).  Per tile it dequantises each of its units into
+    // a slot and lane 0 of its first warp issues that unit's MMAs into the
+    // replica's accumulator (one thread waits about as long per tcgen05.mma as
+    // the tensor core takes for one, so several issuing pairs keep it busy); an
+    // accumulator therefore always grows in tile order.
     const int dw = warp - 4;                       // 0..11
     const int pair = dw >> 1, pl = (dw & 1) * 32 + lane;
     const bool issuer = (dw & 1) == 0 && lane == 0;
+    const int TP = v2_tile_pairs(R), RF = v2_replicas(R), NACT = TP * RF;
+    const int SPP = kV2Abufs / NACT;               // A slots of each active pair
+    const int rep_j = pair / TP, m0 = pair % TP;
     constexpr uint32_t IDESC = (1u << 4) | (1u << 15) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-    int uc = 0;                                    // units this pair processed
+    int ks = 0;                                    // slot index of the next unit (slot pair + NACT * ks)
+    uint32_t kph = 0;                              // its use parity
     bool ok = true;
-    for (int t = 0; t < ntiles && ok; ++t) {
+    const bool active = pair < NACT;
+    // every active warp passes every stage (so none falls a barrier phase behind)
+    // and works on its replica's tiles
+    int s = 0, sph = 0, tr = 0;                    // stage and its parity, t % RF
+    int tb = 0;                                    // B tile t % NB and the parity of its use
+    uint32_t bph = 0;
+    for (int t = 0; active && t < ntiles && ok; ++t, tr = (tr + 1 == RF) ? 0 : tr + 1) {
+      if (t > 0) {
+        if (++s == NS) { s = 0; sph ^= 1; }
+        if (++tb == NB) { tb = 0; bph ^= 1; }
+      }
       if (*s_abort) break;
-      const int s = t % NS, tb = t & 1;
-      if (!mbar_wait(st_full + s, (uint32_t)((t / NS) & 1))) { ok = false; break; }
+      if (!mbar_wait(st_full + s, (uint32_t)sph)) { ok = false; break; }
+      if (tr != rep_j) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(st_empty + s);
+        continue;
+      }
       if (dw == 0 && lane == 0) VTRACE(t, 1);
       const uint8_t* codes = Ssm + (size_t)s * p.stage_bytes;
       const uint8_t* pars = codes + kV2Tile * code_row;
@@ -761,9 +801,11 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       const int pcopied = pend > (pstart & ~(int64_t)15) ? (int)(pend - (pstart & ~(int64_t)15)) : 0;
       const uint8_t* gpars = p.v_params + pstart;
       bool have_b = false;
-      for (int m = pair; m < MU && ok; m += kV2Abufs, ++uc) {
-        const int k = pair;
-        if (!mbar_wait(a_empty + k, (uint32_t)((uc & 1) ^ 1))) { ok = false; break; }
+      for (int m = m0; m < MU && ok; m += kV2Abufs) {
+        const int k = pair + NACT * ks;                      // slot of this unit
+        const uint32_t ph = kph;
+        if (++ks == SPP) { ks = 0; kph ^= 1; }
+        if (!mbar_wait(a_empty + k, ph ^ 1)) { ok = false; break; }
         const int c0 = m * 128;                              // first global channel of the M unit
         const int nch = min(128, R - c0);
         const int gc = nch >> 5;                             // 32-channel groups in the M tile
@@ -778,8 +820,8 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         __syncwarp();
         if (lane == 0) mbar_arrive(a_full + k);
         if (issuer) {
-          bool good = mbar_wait(a_full + k, (uint32_t)(uc & 1));   // both warps of the pair wrote the slot
-          if (good && !have_b) good = mbar_wait(b_full + tb, (uint32_t)((t >> 1) & 1));
+          bool good = mbar_wait(a_full + k, ph);            // both warps of the pair wrote the slot
+          if (good && !have_b) good = mbar_wait(b_full + tb, bph);
           if (!good) {
             fail(kDevWaitMma);
           } else {
@@ -787,21 +829,21 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
             tc_fence_after();
             const uint64_t ad = smem_desc(smem_u32(A), 128, 1024);
             const uint64_t bd = smem_desc(smem_u32(Bsm + tb * p.b_bytes), 128, 1024);
-            const uint32_t d = tmem + (uint32_t)(m * NP);
+            const uint32_t d = tmem + (uint32_t)((rep_j * TP + m) * NP);
 #pragma unroll
             for (int ks = 0; ks < kV2Tile / 16; ++ks)
-              mma_f16_ss(d, ad + (uint64_t)(ks * 16), bd + (uint64_t)(ks * 16), IDESC, (t > 0 || ks > 0) ? 1u : 0u);
+              mma_f16_ss(d, ad + (uint64_t)(ks * 16), bd + (uint64_t)(ks * 16), IDESC, (t > rep_j || ks > 0) ? 1u : 0u);
             mma_commit(a_empty + k);
           }
         }
         __syncwarp();
       }
-      if (issuer && pair < MU) mma_commit(b_empty + tb);    // this pair's reads of the tile's B are queued
+      if (issuer) mma_commit(b_empty + tb);                 // this pair's reads of the tile's B are queued
       __syncwarp();
       if (ok && lane == 0) mbar_arrive(st_empty + s);
       if (dw == 0 && lane == 0) VTRACE(t, 5);
     }
-    if (issuer && pair < MU) mma_commit(fin_bar);          // arrives once this pair's MMAs retired
+    if (issuer && active) mma_commit(fin_bar);              // arrives once this pair's MMAs retired
     if (!ok) fail(kDevWaitMma);
     // ---- epilogue: accumulators -> split partials (warp quarter = TMEM lanes)
     const bool have = ntiles > 0 && !*s_abort;
@@ -812,21 +854,26 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       const int cg = m * 128 + q4 * 32 + (lane & ~7) + v_perm8(lane & 7);   // global channel of this lane's row
       const int blk = cg < R ? s_cblk[cg >> 5] : 0;
       const int Gv = lay.v_num_kv[blk] * qpk, qh0 = lay.v_first_kv[blk] * qpk;
-      float d[NP];
-      const uint32_t ta = tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(m * NP);
-      if (have && !*s_abort) {
-        if constexpr (NP == 16) tmem_ld16(ta, d);
-        else tmem_ld32(ta, d);
-      } else {
-#pragma unroll
-        for (int g = 0; g < NP; ++g) d[g] = 0.f;
-      }
       const int c = cg - lay.v_col[blk];                     // channel within the V block
-      if (cg < R) {
+      const bool rd = have && !*s_abort;
 #pragma unroll
-        for (int g = 0; g < NP; ++g)
-          if (g >= qh0 && g < qh0 + Gv)
-            p.partial[(((int64_t)b * Hq + g) * p.nsplit + split) * p.rv_max + c] = d[g] * (1.f / kVPScale);
+      for (int h = 0; h < NP; h += 16) {                     // 16 heads at a time
+        float d[16];
+#pragma unroll
+        for (int g = 0; g < 16; ++g) d[g] = 0.f;
+        // replicas that received a tile (replica j gets tiles j, j + RF, ...)
+        for (int j = 0; rd && j < RF && j < ntiles; ++j) {
+          float e[16];
+          tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)((j * TP + m) * NP + h), e);
+#pragma unroll
+          for (int g = 0; g < 16; ++g) d[g] += e[g];
+        }
+        if (cg < R) {
+#pragma unroll
+          for (int g = 0; g < 16; ++g)
+            if (h + g >= qh0 && h + g < qh0 + Gv)
+              p.partial[(((int64_t)b * Hq + h + g) * p.nsplit + split) * p.rv_max + c] = d[g] * (1.f / kVPScale);
+        }
       }
     }
   }

@@ -85,6 +85,30 @@ def test_decode_matches_oracle(cuda, cfg, over, mask):
     assert np.abs(out - ref).max() <= MAX_ABS
 
 
+@pytest.mark.parametrize("ranks,context,batch", [
+    ([96], 40, 2),           # one M unit, one tile: five of six accumulator replicas stay empty
+    ([96], 3000, 2),         # one M unit, six replicas
+    ([96], 8000, 16),        # ... with ~14 tiles per V split: every B tile buffer reused
+    ([128, 64], 2000, 2),    # two units, three replicas each
+    ([128, 64], 6000, 16),
+    ([192, 192], 1500, 2),   # three units, two replicas
+    ([192, 192], 6000, 16),
+    ([256, 256], 1500, 2),   # four units, one replica
+    ([320, 320], 900, 2),    # five units
+])
+def test_v_units_and_replicas(cuda, ranks, context, batch):
+    """V layers narrower than six 128-channel units (head shards): the dequant warp
+    pairs split the tiles into per-replica accumulators summed at the end."""
+    spec = make_spec("c1", seed=16, num_q_heads=8, batch=batch, context=context,
+                     v_block_kv=[8 // len(ranks)] * len(ranks), v_ranks=ranks)
+    data = make_layer(spec)
+    ref = O.layer_reference(data)
+    for ns in (0, 1, 5):
+        out, _ = _run(data, cuda, num_splits=ns)
+        assert O.rel_l2(out, ref) <= REL_L2
+        assert np.abs(out - ref).max() <= MAX_ABS
+
+
 def test_split_count_invariance_and_determinism(cuda):
     spec = make_spec("c1", seed=12, num_q_heads=8, batch=2, context=3000)
     data = make_layer(spec)
