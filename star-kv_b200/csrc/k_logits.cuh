@@ -79,7 +79,18 @@ struct KParams {
   int wstride;            // bytes per (sequence, query head) W image
   unsigned long long wait_ns;  // time limit of one device wait
   int skip_unit;          // test hook: the first CTA never issues this unit's copy (-1: off)
+#ifdef STARKV_KTRACE
+  long long* trace;       // diagnostic builds only: clock64 per (job of CTA 0, field), CTA start / end
+#endif
 };
+#ifdef STARKV_KTRACE
+#define KTRACE(j, f)                                                                                  \
+  do {                                                                                                \
+    if (p.trace && blockIdx.x == 0 && (j) < 1024) p.trace[(j) * 16 + (f)] = clock64();               \
+  } while (0)
+#else
+#define KTRACE(j, f) do { } while (0)
+#endif
 
 constexpr int kKThreads = 640;
 // Register budget per warpgroup after setmaxnreg: control, two converters, two
@@ -489,6 +500,9 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+#ifdef STARKV_KTRACE
+  if (tid == 0 && p.trace && blockIdx.x < 1024) p.trace[16384 + blockIdx.x * 2] = (long long)global_timer_ns();
+#endif
   const int NR = *s_nruns;
   const int NT = s_ring[0];                      // tile slots in the ring
   const int TB = s_ring[1];                      // bytes per tile slot
@@ -525,6 +539,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
           if (!skip) {                               // (test hook: a skipped stage never lands)
             mbar_arrive_expect_tx(st_full + slot, bytes);
             bulk_g2s(Ssm + (size_t)ts * TB + s_runoff[n], s_src[g0] + (size_t)t0 * R, bytes, st_full + slot);
+            KTRACE(u, 0);
           }
           if (++n == NR) { n = 0; ++t; }
         }
@@ -557,6 +572,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         if (n >= NR) { n -= NR; ++t; }
         for (int u = iw; u < U && ok; u += NI) {
           if (!mbar_wait(a_full + (u & 1), (uint32_t)((u >> 1) & 1), wlim)) { ok = false; break; }
+          KTRACE(u, 4);
           const uint32_t a_t = tmem + 384u + (uint32_t)(u & 1) * 64u;
           const int g0 = s_run0[n], len = s_runlen[n];
           for (int k = 0; k < len; ++k) {
@@ -565,6 +581,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
               const int jp = j - kKAcc;
               if (!mbar_wait(d_empty + jp % (6 * G), (uint32_t)((jp / (6 * G)) & 1), wlim)) { ok = false; break; }
             }
+            KTRACE(j, 5);
             tc_fence_after();
             const int r = s_rank[g];
             const uint64_t bdesc = smem_desc(smem_u32(Bsm + s_boff[g]), 128, (uint32_t)r * 16u);
@@ -572,6 +589,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
             mma_f16_ts(d, a_t, bdesc, IDESC, 0u);
             for (int kk = 1; kk < (r >> 4); ++kk) mma_f16_ts(d, a_t + kk * 8, bdesc + (uint64_t)(kk * 16), IDESC, 1u);
             mma_commit(d_full + j % (6 * G));
+            KTRACE(j, 6);
           }
           mma_commit(a_empty + (u & 1));
           n += NI;
@@ -631,6 +649,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         const int g0 = s_run0[n], r = s_rank[g0];
         const int ts = t % NT, s = ts * NR + n;
         if (!mbar_wait(st_full + s, (uint32_t)((t / NT) & 1), wlim)) { fail(kDevWaitCopy); break; }
+        if (ct == 0) KTRACE(u, 1);
         const int rc = (r * XB) >> 4;
         const int cs = tiled ? 2048 : 16;            // bytes between a row's 16-byte chunks
         const uint8_t* srow = Ssm + (size_t)ts * TB + s_runoff[n] + (size_t)ct * (tiled ? 16 : r * XB);
@@ -642,6 +661,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         auto wait_a = [&]() -> bool {              // the A buffer's previous MMAs retired
           if (!mbar_wait(a_empty + cw, (uint32_t)(((u >> 1) & 1) ^ 1), wlim)) { fail(kDevWaitMma); return false; }
           tc_fence_after();
+          if (ct == 0) KTRACE(u, 2);
           return true;
         };
         bool okc = true;
@@ -669,6 +689,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(a_full + cw);
+        if (ct == 0) KTRACE(u, 3);
         n += 2;
         while (n >= NR) { n -= NR; ++t; }
       }
@@ -720,6 +741,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
           const float madd = (p.mask && live) ? p.mask[(int64_t)b * p.T + l] * p.mask_scale : 0.f;
           float* const dst = lg_base + (int64_t)g * p.T + tile * 128;
           if (!mbar_wait(d_full + ds, (uint32_t)((j / (6 * G)) & 1), wlim)) { ok = false; break; }
+          if (row == 0) KTRACE(j, 7);
           tc_fence_after();
           const uint32_t ta = lbase + (uint32_t)db * 128u;
           float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
@@ -731,6 +753,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
               tc_fence_before();
               __syncwarp();
               if (lane == 0) mbar_arrive(d_empty + ds);
+              if (row == 0) KTRACE(j, 8);
             }
             const int f0 = (q & 3) * 8;                  // first frequency pair of this block
 #pragma unroll
@@ -752,6 +775,7 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
             for (int gg = 0; gg < G; ++gg)
               if (gg == g) m_run[gg] = fmaxf(m_run[gg], val);
           }
+          if (row == 0) KTRACE(j, 9);
         }
       }
       if (!ok) fail(kDevWaitMma);
@@ -779,6 +803,9 @@ __global__ void __launch_bounds__(kKThreads, 1) k_logits_kernel(const __grid_con
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+#ifdef STARKV_KTRACE
+  if (tid == 0 && p.trace && blockIdx.x < 1024) p.trace[16384 + blockIdx.x * 2 + 1] = (long long)global_timer_ns();
+#endif
 }
 
 }  // namespace starkv

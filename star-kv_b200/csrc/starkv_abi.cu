@@ -22,6 +22,9 @@ thread_local char g_last_error[256] = "";
 // K-kernel stage whose copy is never issued.
 unsigned long long g_wait_ns = kWaitLimitNs;
 int g_skip_unit = -1;
+#ifdef STARKV_KTRACE
+long long* g_ktrace = nullptr;   // diagnostic builds only
+#endif
 
 int fail_launch() {
   const cudaError_t e = cudaGetLastError();
@@ -398,6 +401,9 @@ int prepare_k(const starkv_layout* lay, const starkv_decode_args* a, KParams& kp
   kp.inv_freq = a->inv_freq;
   kp.wait_ns = g_wait_ns;
   kp.skip_unit = g_skip_unit;
+#ifdef STARKV_KTRACE
+  kp.trace = g_ktrace;
+#endif
   return STARKV_OK;
 }
 
@@ -744,6 +750,15 @@ int starkv_quantize_split(const void* x, int32_t dtype, int64_t rows, int32_t r,
   }
   return fail_launch();
 }
+
+#ifdef STARKV_KTRACE
+// Diagnostic builds only: K kernel timeline buffer (16 x 1024 job stamps of CTA 0,
+// then start / end of CTAs 0..1023), or null to stop.
+extern "C" int starkv_debug_ktrace(void* buf) {
+  g_ktrace = reinterpret_cast<long long*>(buf);
+  return STARKV_OK;
+}
+#endif
 
 int starkv_set_test_hooks(int64_t wait_limit_ns, int32_t skip_copy_unit) {
   g_wait_ns = wait_limit_ns > 0 ? (unsigned long long)wait_limit_ns : kWaitLimitNs;
