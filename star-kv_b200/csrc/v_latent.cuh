@@ -768,6 +768,12 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
     const int TP = v2_tile_pairs(R), RF = v2_replicas(R), NACT = TP * RF;
     const int SPP = kV2Abufs / NACT;               // A slots of each active pair
     const int rep_j = pair / TP, m0 = pair % TP;
+    // Rotating tail: with U = 6q + rem units (q >= 1, 0 < rem < 6), units below 6q keep
+    // their owner pairs and tail unit i goes to pair (t * rem + i) mod 6 in tile t, into
+    // that pair's own accumulator for it (summed in the epilogue), so every pair
+    // dequantises about U / 6 units per tile (when the 6q + 6 rem accumulators fit TMEM).
+    const int q6 = (MU / 6) * 6, rem = MU - q6;
+    const bool TAIL = RF == 1 && q6 > 0 && rem > 0 && (q6 + 6 * rem) * NP <= 512;
     constexpr uint32_t IDESC = (1u << 4) | (1u << 15) | ((uint32_t)(NP >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
     int ks = 0;                                    // slot index of the next unit (slot pair + NACT * ks)
     uint32_t kph = 0;                              // its use parity
@@ -778,10 +784,13 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
     int s = 0, sph = 0, tr = 0;                    // stage and its parity, t % RF
     int tb = 0;                                    // B tile t % NB and the parity of its use
     uint32_t bph = 0;
+    int trot = 0;                                  // (t * rem) mod 6
+    uint32_t tinit = 0;                            // tail accumulators of this pair already written
     for (int t = 0; active && t < ntiles && ok; ++t, tr = (tr + 1 == RF) ? 0 : tr + 1) {
       if (t > 0) {
         if (++s == NS) { s = 0; sph ^= 1; }
         if (++tb == NB) { tb = 0; bph ^= 1; }
+        trot = (trot + rem) % 6;
       }
       if (*s_abort) break;
       if (!mbar_wait(st_full + s, (uint32_t)sph)) { ok = false; break; }
@@ -801,7 +810,26 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
       const int pcopied = pend > (pstart & ~(int64_t)15) ? (int)(pend - (pstart & ~(int64_t)15)) : 0;
       const uint8_t* gpars = p.v_params + pstart;
       bool have_b = false;
-      for (int m = m0; m < MU && ok; m += kV2Abufs) {
+      int own_m = m0, ti = 0;
+      const int nown = TAIL ? q6 : MU;
+      while (ok) {
+        int m, dcol;                                         // unit, its accumulator's first column
+        bool first;                                          // first tile into that accumulator
+        if (own_m < nown) {
+          m = own_m;
+          own_m += kV2Abufs;
+          dcol = (rep_j * TP + m) * NP;
+          first = t == rep_j;
+        } else {
+          if (!TAIL) break;
+          while (ti < rem && (trot + ti) % 6 != pair) ++ti;
+          if (ti >= rem) break;
+          m = q6 + ti;
+          dcol = (q6 + pair * rem + ti) * NP;
+          first = ((tinit >> ti) & 1u) == 0;
+          tinit |= 1u << ti;
+          ++ti;
+        }
         const int k = pair + NACT * ks;                      // slot of this unit
         const uint32_t ph = kph;
         if (++ks == SPP) { ks = 0; kph ^= 1; }
@@ -829,10 +857,10 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
             tc_fence_after();
             const uint64_t ad = smem_desc(smem_u32(A), 128, 1024);
             const uint64_t bd = smem_desc(smem_u32(Bsm + tb * p.b_bytes), 128, 1024);
-            const uint32_t d = tmem + (uint32_t)((rep_j * TP + m) * NP);
+            const uint32_t d = tmem + (uint32_t)dcol;
 #pragma unroll
-            for (int ks = 0; ks < kV2Tile / 16; ++ks)
-              mma_f16_ss(d, ad + (uint64_t)(ks * 16), bd + (uint64_t)(ks * 16), IDESC, (t > rep_j || ks > 0) ? 1u : 0u);
+            for (int kk = 0; kk < kV2Tile / 16; ++kk)
+              mma_f16_ss(d, ad + (uint64_t)(kk * 16), bd + (uint64_t)(kk * 16), IDESC, (!first || kk > 0) ? 1u : 0u);
             mma_commit(a_empty + k);
           }
         }
@@ -861,10 +889,24 @@ __global__ void __launch_bounds__(kV2Threads, 1) v_decode_kernel(const __grid_co
         float d[16];
 #pragma unroll
         for (int g = 0; g < 16; ++g) d[g] = 0.f;
-        // replicas that received a tile (replica j gets tiles j, j + RF, ...)
-        for (int j = 0; rd && j < RF && j < ntiles; ++j) {
+        // the unit's accumulators that received a tile: replica j of an owned unit
+        // gets tiles j, j + RF, ...; pair cand's copy of tail unit i the tiles with
+        // (t * rem + i) mod 6 == cand (a pattern of period <= 6)
+        const bool tail_m = TAIL && m >= q6;
+        const int ncand = tail_m ? 6 : RF;
+        for (int cand = 0; rd && cand < ncand; ++cand) {
+          bool use = false;
+          int col;
+          if (tail_m) {
+            for (int tt = 0; tt < ntiles && tt < 6; ++tt) use |= (tt * rem + (m - q6)) % 6 == cand;
+            col = (q6 + cand * rem + (m - q6)) * NP;
+          } else {
+            use = cand < ntiles;
+            col = (cand * TP + m) * NP;
+          }
+          if (!use) continue;
           float e[16];
-          tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)((j * TP + m) * NP + h), e);
+          tmem_ld16(tmem + ((uint32_t)(q4 * 32) << 16) + (uint32_t)(col + h), e);
 #pragma unroll
           for (int g = 0; g < 16; ++g) d[g] += e[g];
         }

@@ -95,12 +95,21 @@ def test_decode_matches_oracle(cuda, cfg, over, mask):
     ([192, 192], 6000, 16),
     ([256, 256], 1500, 2),   # four units, one replica
     ([320, 320], 900, 2),    # five units
+    # seven, ten and thirteen units: the units past the last multiple of six rotate
+    # over the pairs tile by tile (rotating tail), each pair with its own accumulator
+    ([256, 256, 256, 64], 1500, 2),
+    ([256, 256, 256, 64], 6000, 16),
+    ([256, 256, 256, 256, 128, 96], 3000, 4),
+    ([256, 256, 256, 256, 256, 256, 64], 2000, 4),
 ])
 def test_v_units_and_replicas(cuda, ranks, context, batch):
-    """V layers narrower than six 128-channel units (head shards): the dequant warp
-    pairs split the tiles into per-replica accumulators summed at the end."""
+    """V layers whose 128-channel units do not fill six dequant warp pairs evenly:
+    fewer than six units (head shards) split the tiles into per-replica
+    accumulators; past a multiple of six the tail units rotate over the pairs."""
+    nb = len(ranks)
+    blocks = [8 // nb + (1 if j < 8 % nb else 0) for j in range(nb)]
     spec = make_spec("c1", seed=16, num_q_heads=8, batch=batch, context=context,
-                     v_block_kv=[8 // len(ranks)] * len(ranks), v_ranks=ranks)
+                     v_block_kv=blocks, v_ranks=ranks)
     data = make_layer(spec)
     ref = O.layer_reference(data)
     for ns in (0, 1, 5):
