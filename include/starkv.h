@@ -258,6 +258,40 @@ int starkv_set_test_hooks(int64_t wait_limit_ns, int32_t skip_copy_unit);
  * (synchronises the stream); *out_code = 0 means no device-side error. */
 int starkv_read_device_error(void* workspace, int* out_code, starkv_stream_t stream);
 
+/*
+ * Causal prompt (prefill) attention over K / V rebuilt from the latents: the
+ * SDPA call of the reference's prompt path (model.py:429-449,
+ * LlamaLoRaAttention_headwise.py:100-116: F.scaled_dot_product_attention with
+ * is_causal over RoPE(X_k U_k^T) and X_v U_v^T, GQA by repeat_kv).  q (B, Hq, T,
+ * 128) rotated queries, k (B, Hkv, T, 128) rotated keys, v (B, Hkv, T, 128), all
+ * of `dtype` (fp16 / bf16) with arbitrary element strides (batch, head, token;
+ * multiples of 8, 16-byte aligned bases, the 128 channels contiguous), so the
+ * projections' (B, T, H, 128) tensors are read in place.  Query t attends to
+ * keys [0, t]; query head h uses KV head h / (Hq / Hkv).  out (B, Hq, T, 128) of
+ * out_dtype with its own strides.  error_word (nullable): device int that a
+ * timed-out device wait sets (see starkv_read_device_error).  Allocates nothing.
+ */
+typedef struct starkv_prefill_args {
+  const void* q;
+  const void* k;
+  const void* v;
+  int64_t q_strides[3];     /* elements: batch, head, token */
+  int64_t k_strides[3];
+  int64_t v_strides[3];
+  int32_t dtype;            /* STARKV_F16 or STARKV_BF16 */
+  int32_t batch;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t num_tokens;
+  float scaling;            /* softmax scale, head_dim^-0.5 in the reference */
+  void* out;
+  int32_t out_dtype;
+  int64_t out_strides[3];
+  int* error_word;
+} starkv_prefill_args;
+
+int starkv_prefill_attention(const starkv_prefill_args* args, starkv_stream_t stream);
+
 /* Last CUDA error string seen by the library on this thread (for diagnostics). */
 const char* starkv_last_error(void);
 

@@ -220,6 +220,44 @@ def decode_attention(q_rot, xk, k_u, xv, v_u_weight, k_ranks, v_ranks, v_block_o
             out[:, h, :] = o_lat @ u_h.T                                      # :128-130
     return out
 
+def prompt_attention(q_rot, xk, k_u, xv, v_u_weight, k_ranks, v_ranks, v_block_of_kv,
+                     inv_freq, scaling, dtype=np.float64):
+    """Causal prompt (prefill) attention over K / V rebuilt from unquantised latents.
+
+    Restates the reference's prefill branch (model.py:429-449): key_full =
+    RoPE(X_k @ U_k^T) at positions 0..T-1 (:431-432), GQA repeat of the K / V heads
+    (:436, :442), value_full = X_v @ v_proj.U.weight^T split into heads (:437-441),
+    then softmax(q k^T * scaling) v with query t attending to keys 0..t (SDPA with
+    the model's causal mask, :443-449).
+
+    q_rot: (B, Hq, T, 128) rotated queries; xk: list over KV heads of (B, T, r_h);
+    k_u: list of (128, r_h); xv: (B, T, sum r_b); v_u_weight (Hkv*128, sum r_b).
+    Returns (B, Hq, T, 128) in ``dtype``.
+    """
+    B, Hq, T, D = q_rot.shape
+    Hkv = len(xk)
+    grp = Hq // Hkv
+    cos, sin = rope_cos_sin(np.arange(T), inv_freq)
+    cos, sin = cos.astype(dtype), sin.astype(dtype)
+    vcol = np.concatenate([[0], np.cumsum(v_ranks)]).astype(np.int64)
+    causal = np.tril(np.ones((T, T), dtype=bool))
+    out = np.zeros((B, Hq, T, D), dtype=dtype)
+    for kv in range(Hkv):
+        keys = apply_rope(np.matmul(xk[kv].astype(dtype), k_u[kv].astype(dtype).T), cos[None], sin[None])
+        j = v_block_of_kv[kv]
+        vals = np.matmul(xv[:, :, vcol[j]:vcol[j + 1]].astype(dtype),
+                         v_u_weight[kv * D:(kv + 1) * D, vcol[j]:vcol[j + 1]].astype(dtype).T)   # (B, T, 128)
+        for g in range(grp):
+            h = kv * grp + g
+            logits = np.matmul(q_rot[:, h].astype(dtype), keys.transpose(0, 2, 1)) * dtype(scaling)
+            logits = np.where(causal[None], logits, -np.inf)
+            logits -= logits.max(axis=-1, keepdims=True)
+            p = np.exp(logits)
+            p /= p.sum(axis=-1, keepdims=True)
+            out[:, h] = np.matmul(p, vals)
+    return out
+
+
 
 def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
     a = np.asarray(a, dtype=np.float64)

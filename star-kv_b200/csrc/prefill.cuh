@@ -1,0 +1,367 @@
+// prefill.cuh — prompt (prefill) attention on the 5th-generation tensor cores.
+//
+// The reference's prompt path rebuilds full K / V from the latents
+// (K = RoPE(X_k U_k^T), V = X_v U_v^T) and runs causal SDPA over them
+// (model.py:429-449, LlamaLoRaAttention_headwise.py:100-116).  This kernel is the
+// attention half of that: causal flash attention with the online softmax, one
+// CTA per (128-query tile, query head, sequence), K / V of the query head's KV
+// head (GQA by index), q / k / v / out as strided (B, H, T, 128) views so that
+// the projections' (B, T, H, 128) tensors are read and written in place.
+//
+// Roles (256 threads, one CTA per SM: it holds all 512 TMEM columns):
+//   * warps 0-3 (thread = query row): softmax.  S_j = Q K_j^T lands in TMEM
+//     (fp32, 128 columns, two buffers); the row maximum and exp2 weights are
+//     formed in two passes over S_j, P_j is written back to TMEM as the 16-bit A
+//     operand (64 columns, two buffers), and the previous tile's P V result is
+//     folded into the fp32 output row kept in registers (o = o * alpha + pv).
+//   * warp 4, one thread: tcgen05.mma issue.  S_{j+1} is issued before waiting
+//     for P_j so that the tensor core computes the next logits while the
+//     softmax warps work; P_j V_j goes into one 128-column accumulator.
+//   * warps 5-7: cp.async staging of the Q tile and of a two-stage ring of
+//     (K_j, V_j) tiles, 16-byte chunks written straight into the canonical
+//     no-swizzle layouts (K and Q K-major, V MN-major: no transposition).
+// Every mbarrier wait is bounded; a wait that runs out records an error code,
+// sets the CTA's abort flag and the roles leave their loops.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace starkv {
+
+constexpr int kPfThreads = 256;
+constexpr int kPfTile = 128;                    // queries per CTA and keys per step
+constexpr int kPfTileBytes = 128 * 128 * 2;     // one 128 x 128 16-bit tile
+constexpr int kPfHeader = 1024;                 // barriers + TMEM address + abort flag
+constexpr size_t kPfSmem = kPfHeader + 5 * (size_t)kPfTileBytes;   // Q + 2 x (K, V)
+
+// TMEM columns: S buffers, the P V accumulator and the P buffers (16-bit pairs).
+constexpr uint32_t kPfColS = 0, kPfColO = 256, kPfColP = 384;
+
+struct PrefillParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* out;
+  int64_t q_stride[3];     // elements: batch, head, token (the 128 channels are contiguous)
+  int64_t k_stride[3];
+  int64_t v_stride[3];
+  int64_t o_stride[3];
+  int batch, num_q_heads, num_kv_heads, num_tokens, n_qtiles;
+  int out_dtype;
+  float scale_log2;        // softmax scale * log2(e)
+  int* err;                // device error word (nullable)
+  unsigned long long wait_ns;
+};
+
+// Instruction descriptor, kind::f16 with A = B = 16-bit type T, D = f32, A K-major,
+// B K-major (b_mn = false) or MN-major (b_mn = true), M = N = 128.
+template <typename T>
+__host__ __device__ constexpr uint32_t idesc_pf(bool b_mn) {
+  constexpr uint32_t fmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(128 >> 3) << 17) |
+         ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 16-byte cp.async that reads src_bytes (0 or 16) and zero-fills the rest.
+__device__ __forceinline__ void cp_async16_zfill(void* dst_smem, const void* src_gmem, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst_smem)), "l"(src_gmem),
+               "r"(src_bytes)
+               : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Stage one 128-row tile (rows [row0, row0+128) of a strided (T, 128) matrix,
+// rows >= T zero) into the canonical no-swizzle layout.  Chunk c (16 bytes) of
+// the tile lands at byte 16*c.  K-major (Q, K: row = M/N index, 8 channels per
+// chunk): row = c%8 + 8*(c/128), channel block = (c/8)%16.  MN-major (V: the 8
+// channels of a chunk run along N, the token along K): token = c%8 + 8*((c/8)%16),
+// channel block = c/128.
+template <bool MN>
+__device__ __forceinline__ void pf_stage_tile(uint8_t* dst, const uint8_t* src, int64_t row_stride_bytes,
+                                              int row0, int T, int tid, int nthreads) {
+  for (int c = tid; c < 2048; c += nthreads) {
+    int row, blk;
+    if (MN) {
+      row = (c & 7) + 8 * ((c >> 3) & 15);
+      blk = c >> 7;
+    } else {
+      row = (c & 7) + 8 * (c >> 7);
+      blk = (c >> 3) & 15;
+    }
+    const int gr = row0 + row;
+    const bool ok = gr < T;
+    const uint8_t* s = src + (int64_t)(ok ? gr : 0) * row_stride_bytes + blk * 16;
+    cp_async16_zfill(dst + 16 * c, s, ok ? 16u : 0u);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const PrefillParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;     // [2]
+  uint64_t* kv_empty = bar + 3;    // [2]
+  uint64_t* s_full = bar + 5;      // [2]
+  uint64_t* p_full = bar + 7;      // [2]
+  uint64_t* o_full = bar + 9;
+  uint64_t* o_free = bar + 10;
+  uint64_t* mma_done = bar + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 256);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 260);
+  uint8_t* Qs = smem + kPfHeader;
+  uint8_t* KVs = Qs + kPfTileBytes;    // stage s: K at 2*s, V at 2*s+1 tiles
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int per = p.num_q_heads * p.batch;
+  const int cta = blockIdx.x;
+  const int qt = p.n_qtiles - 1 - cta / per;      // heaviest query tiles first
+  const int h = (cta % per) % p.num_q_heads;
+  const int b = (cta % per) / p.num_q_heads;
+  const int kvh = h / (p.num_q_heads / p.num_kv_heads);
+  const int n = qt + 1;                            // causal: key tiles 0..qt
+  const unsigned long long lim = p.wait_ns;
+
+  if (tid == 0) {
+    mbar_init(q_full, 96);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(kv_full + s, 96);
+      mbar_init(kv_empty + s, 1);
+      mbar_init(s_full + s, 1);
+      mbar_init(p_full + s, 128);
+    }
+    mbar_init(o_full, 1);
+    mbar_init(o_free, 128);
+    mbar_init(mma_done, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto wait = [&](uint64_t* bar_, uint32_t parity, int code) -> bool {
+    if (*s_abort) return false;
+    if (mbar_wait(bar_, parity, lim)) return true;
+    record_error(p.err, code);
+    *s_abort = 1;
+    return false;
+  };
+
+  if (warp >= 5) {
+    // ---------------------------------------------------------------- producer
+    const int pt = tid - 160;
+    const uint8_t* qsrc = reinterpret_cast<const uint8_t*>(p.q) +
+                          2 * (b * p.q_stride[0] + h * p.q_stride[1]);
+    const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(p.k) +
+                          2 * (b * p.k_stride[0] + kvh * p.k_stride[1]);
+    const uint8_t* vsrc = reinterpret_cast<const uint8_t*>(p.v) +
+                          2 * (b * p.v_stride[0] + kvh * p.v_stride[1]);
+    const int64_t qrs = 2 * p.q_stride[2], krs = 2 * p.k_stride[2], vrs = 2 * p.v_stride[2];
+    pf_stage_tile<false>(Qs, qsrc, qrs, qt * kPfTile, p.num_tokens, pt, 96);
+    cp_async_commit();
+    auto issue = [&](int j) {
+      uint8_t* st = KVs + (size_t)(j & 1) * 2 * kPfTileBytes;
+      pf_stage_tile<false>(st, ksrc, krs, j * kPfTile, p.num_tokens, pt, 96);
+      pf_stage_tile<true>(st + kPfTileBytes, vsrc, vrs, j * kPfTile, p.num_tokens, pt, 96);
+      cp_async_commit();
+    };
+    // Tile j is announced before the producer waits to refill a stage with tile
+    // j+1: the MMA thread needs tile j (for S_j) before it issues P_{j-1} V_{j-1},
+    // the MMAs whose completion frees that stage.
+    issue(0);
+    if (n > 1) {
+      issue(1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    fence_proxy_async_smem();
+    mbar_arrive(q_full);
+    mbar_arrive(kv_full);
+    for (int j = 1; j < n; ++j) {
+      cp_async_wait<0>();
+      fence_proxy_async_smem();
+      mbar_arrive(kv_full + (j & 1));
+      if (j + 1 < n) {
+        if (!wait(kv_empty + ((j + 1) & 1), (((j + 1) >> 1) - 1) & 1, kDevWaitMma)) break;
+        issue(j + 1);
+      }
+    }
+    cp_async_wait<0>();
+  } else if (warp == 4) {
+    // ------------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      constexpr uint32_t IS = idesc_pf<T>(false), IO = idesc_pf<T>(true);
+      const uint32_t qa = smem_u32(Qs);
+      auto issue_s = [&](int j) {
+        const uint32_t kb = smem_u32(KVs + (size_t)(j & 1) * 2 * kPfTileBytes);
+        const uint32_t d = tmem + kPfColS + (uint32_t)(j & 1) * 128;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ss(d, smem_desc(qa + kk * 256, 128, 2048), smem_desc(kb + kk * 256, 128, 2048), IS,
+                     kk > 0 ? 1u : 0u);
+        mma_commit(s_full + (j & 1));
+      };
+      bool ok = wait(q_full, 0, kDevWaitCopy) && wait(kv_full, 0, kDevWaitCopy);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; ok && j < n; ++j) {
+        if (j + 1 < n) {
+          if (!wait(kv_full + ((j + 1) & 1), ((j + 1) >> 1) & 1, kDevWaitCopy)) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
+        if (!wait(p_full + (j & 1), (j >> 1) & 1, kDevWaitMma)) break;
+        if (j >= 1 && !wait(o_free, (j - 1) & 1, kDevWaitMma)) break;
+        tc_fence_after();
+        const uint32_t vb = smem_u32(KVs + (size_t)(j & 1) * 2 * kPfTileBytes + kPfTileBytes);
+        const uint32_t pa = tmem + kPfColP + (uint32_t)(j & 1) * 64;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ts(tmem + kPfColO, pa + kk * 8, smem_desc(vb + kk * 256, 128, 2048), IO, kk > 0 ? 1u : 0u);
+        mma_commit(o_full);
+        mma_commit(kv_empty + (j & 1));
+      }
+      // every issued MMA has finished before TMEM is released
+      mma_commit(mma_done);
+      mbar_wait(mma_done, 0, lim);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- softmax
+    const int row = tid;                             // TMEM lane == query row
+    const int qpos = qt * kPfTile + row;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    float o[128];
+#pragma unroll
+    for (int i = 0; i < 128; ++i) o[i] = 0.f;
+    float m_run = kNegBig, l_run = 0.f, alpha_prev = 0.f;
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    auto fold = [&](int j) -> bool {                 // o = o * alpha_j + (P_j V_j)
+      if (!__all_sync(0xffffffffu, wait(o_full, j & 1, kDevWaitMma))) return false;
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tmem_ld16(tmem + lane_base + kPfColO + c * 16, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) o[c * 16 + i] = fmaf(o[c * 16 + i], alpha_prev, v[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(o_free);
+      return true;
+    };
+    for (int j = 0; j < n; ++j) {
+      if (!__all_sync(0xffffffffu, wait(s_full + (j & 1), (j >> 1) & 1, kDevWaitMma))) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t sa = tmem + lane_base + kPfColS + (uint32_t)(j & 1) * 128;
+      const bool diag = (j == qt);
+      const int kmax = diag ? row : 127;               // last kept key column of this row
+      float mx = kNegBig;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tmem_ld16(sa + c * 16, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) mx = (c * 16 + i <= kmax) ? fmaxf(mx, v[i]) : mx;
+      }
+      const float m_new = fmaxf(m_run, mx * sl2);
+      const float alpha = fast_exp2(m_run - m_new);
+      float lsum = 0.f;
+      const uint32_t pcol = tmem + lane_base + kPfColP + (uint32_t)(j & 1) * 64;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tmem_ld16(sa + c * 16, v);
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 16; i += 2) {
+          const float p0 = (c * 16 + i <= kmax) ? fast_exp2(fmaf(v[i], sl2, -m_new)) : 0.f;
+          const float p1 = (c * 16 + i + 1 <= kmax) ? fast_exp2(fmaf(v[i + 1], sl2, -m_new)) : 0.f;
+          lsum += p0 + p1;
+          pk[i >> 1] = pack2<T>(p0, p1);
+        }
+        tmem_st8(pcol + c * 8, pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full + (j & 1));
+      l_run = fmaf(l_run, alpha, lsum);
+      m_run = m_new;
+      if (j >= 1 && !fold(j - 1)) { ok = false; break; }
+      alpha_prev = alpha;
+    }
+    if (ok && n >= 1) ok = fold(n - 1);
+    if (ok && qpos < p.num_tokens) {
+      const float inv = 1.f / l_run;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) o[i] *= inv;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(p.out);
+      const int64_t base = b * p.o_stride[0] + h * p.o_stride[1] + (int64_t)qpos * p.o_stride[2];
+      if (p.out_dtype == STARKV_F32) {
+        float4* d4 = reinterpret_cast<float4*>(dst + 4 * base);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          d4[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+      } else {
+        uint4* d4 = reinterpret_cast<uint4*>(dst + 2 * base);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          uint4 w;
+          if (p.out_dtype == STARKV_BF16) {
+            w.x = pack2<__nv_bfloat16>(o[8 * i], o[8 * i + 1]);
+            w.y = pack2<__nv_bfloat16>(o[8 * i + 2], o[8 * i + 3]);
+            w.z = pack2<__nv_bfloat16>(o[8 * i + 4], o[8 * i + 5]);
+            w.w = pack2<__nv_bfloat16>(o[8 * i + 6], o[8 * i + 7]);
+          } else {
+            w.x = pack2<__half>(o[8 * i], o[8 * i + 1]);
+            w.y = pack2<__half>(o[8 * i + 2], o[8 * i + 3]);
+            w.z = pack2<__half>(o[8 * i + 4], o[8 * i + 5]);
+            w.w = pack2<__half>(o[8 * i + 6], o[8 * i + 7]);
+          }
+          d4[i] = w;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace starkv

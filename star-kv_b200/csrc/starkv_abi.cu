@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "k_logits.cuh"
+#include "prefill.cuh"
 #include "quant.cuh"
 #include "sm100.cuh"
 #include "v_latent.cuh"
@@ -858,6 +859,68 @@ int starkv_decode_attention_static(const starkv_layout* lay, const starkv_decode
   a.workspace = scratch;
   a.workspace_bytes = kStaticScratchBytes;
   return starkv_decode_attention(lay, &a, stream);
+}
+
+int starkv_prefill_attention(const starkv_prefill_args* a, starkv_stream_t stream) {
+  if (!a || !a->q || !a->k || !a->v || !a->out) return set_error(STARKV_ERR_INVALID, "null argument");
+  if (a->dtype != STARKV_F16 && a->dtype != STARKV_BF16)
+    return set_error(STARKV_ERR_UNSUPPORTED, "prefill attention takes fp16 or bf16 q / k / v");
+  if (a->out_dtype != STARKV_F16 && a->out_dtype != STARKV_BF16 && a->out_dtype != STARKV_F32)
+    return set_error(STARKV_ERR_INVALID, "bad out_dtype");
+  if (a->batch <= 0 || a->num_q_heads <= 0 || a->num_kv_heads <= 0 || a->num_tokens <= 0 ||
+      a->num_q_heads % a->num_kv_heads != 0)
+    return set_error(STARKV_ERR_INVALID, "bad batch / head / token counts");
+  const int64_t* strides[3] = {a->q_strides, a->k_strides, a->v_strides};
+  const void* ptrs[3] = {a->q, a->k, a->v};
+  for (int i = 0; i < 3; ++i) {
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16 != 0)
+      return set_error(STARKV_ERR_INVALID, "q / k / v must be 16-byte aligned");
+    for (int d = 0; d < 3; ++d)
+      if (strides[i][d] % 8 != 0 || strides[i][d] < 0)
+        return set_error(STARKV_ERR_INVALID, "q / k / v strides must be non-negative multiples of 8 elements");
+  }
+  const int oe = a->out_dtype == STARKV_F32 ? 4 : 8;
+  if (reinterpret_cast<uintptr_t>(a->out) % 16 != 0)
+    return set_error(STARKV_ERR_INVALID, "out must be 16-byte aligned");
+  for (int d = 0; d < 3; ++d)
+    if (a->out_strides[d] % oe != 0 || a->out_strides[d] < 0)
+      return set_error(STARKV_ERR_INVALID, "out strides must be non-negative multiples of 16 bytes");
+  int rc = check_device();
+  if (rc) return rc;
+  PrefillParams p;
+  memset(&p, 0, sizeof(p));
+  p.q = a->q;
+  p.k = a->k;
+  p.v = a->v;
+  p.out = a->out;
+  for (int d = 0; d < 3; ++d) {
+    p.q_stride[d] = a->q_strides[d];
+    p.k_stride[d] = a->k_strides[d];
+    p.v_stride[d] = a->v_strides[d];
+    p.o_stride[d] = a->out_strides[d];
+  }
+  p.batch = a->batch;
+  p.num_q_heads = a->num_q_heads;
+  p.num_kv_heads = a->num_kv_heads;
+  p.num_tokens = a->num_tokens;
+  p.n_qtiles = (a->num_tokens + kPfTile - 1) / kPfTile;
+  p.out_dtype = a->out_dtype;
+  p.scale_log2 = a->scaling * 1.4426950408889634f;
+  p.err = a->error_word;
+  p.wait_ns = g_wait_ns;
+  const int64_t ctas = (int64_t)p.n_qtiles * a->num_q_heads * a->batch;
+  if (ctas > 0x7fffffff) return set_error(STARKV_ERR_UNSUPPORTED, "too many query tiles");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (a->dtype == STARKV_F16) {
+    rc = ensure_smem(prefill_attn_kernel<__half>, kPfSmem, 20);
+    if (rc) return rc;
+    prefill_attn_kernel<__half><<<(unsigned)ctas, kPfThreads, kPfSmem, st>>>(p);
+  } else {
+    rc = ensure_smem(prefill_attn_kernel<__nv_bfloat16>, kPfSmem, 21);
+    if (rc) return rc;
+    prefill_attn_kernel<__nv_bfloat16><<<(unsigned)ctas, kPfThreads, kPfSmem, st>>>(p);
+  }
+  return fail_launch();
 }
 
 }  // extern "C"

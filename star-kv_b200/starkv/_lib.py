@@ -50,6 +50,19 @@ class DecodeArgs(C.Structure):
     ]
 
 
+class PrefillArgs(C.Structure):
+    """Mirror of ``starkv_prefill_args``."""
+
+    _fields_ = [
+        ("q", C.c_void_p), ("k", C.c_void_p), ("v", C.c_void_p),
+        ("q_strides", C.c_int64 * 3), ("k_strides", C.c_int64 * 3), ("v_strides", C.c_int64 * 3),
+        ("dtype", C.c_int32), ("batch", C.c_int32), ("num_q_heads", C.c_int32), ("num_kv_heads", C.c_int32),
+        ("num_tokens", C.c_int32), ("scaling", C.c_float),
+        ("out", C.c_void_p), ("out_dtype", C.c_int32), ("out_strides", C.c_int64 * 3),
+        ("error_word", C.c_void_p),
+    ]
+
+
 # (name, restype, argtypes) of every exported symbol; tests check the header declares exactly these.
 SIGNATURES = [
     ("starkv_layout_size", C.c_size_t, []),
@@ -74,6 +87,7 @@ SIGNATURES = [
     ("starkv_static_scratch_bytes", C.c_size_t, []),
     ("starkv_static_read_device_error", C.c_int, [C.POINTER(C.c_int), C.c_void_p]),
     ("starkv_read_device_error", C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.c_void_p]),
+    ("starkv_prefill_attention", C.c_int, [C.POINTER(PrefillArgs), C.c_void_p]),
     ("starkv_last_error", C.c_char_p, []),
 ]
 

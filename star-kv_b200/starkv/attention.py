@@ -38,7 +38,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import ops
+from . import ops, prefill
 from .layer import DecodeLayer, rope_inv_freq
 
 
@@ -269,10 +269,19 @@ class LlamaCustomAttention(nn.Module):
                                     mask=self._decode_mask(attention_mask, B, L))
 
     def _prompt_attention(self, q, keys, values, cos, sin, attention_mask):
-        """Prompt (q_len > 1) attention with torch SDPA on reconstructed K/V
-        (model.py:429-449)."""
+        """Prompt (q_len > 1) attention on K/V reconstructed from the latents
+        (model.py:429-449).  A causal prompt from position 0 (no explicit mask) runs
+        the library's tcgen05 flash-attention kernel (``starkv.prefill``); an explicit
+        additive mask, or queries that continue an earlier prompt, go to torch SDPA
+        with that mask, as the reference does."""
         B, Hq, Lq, D = q.shape
         Hkv = self.num_key_value_heads
+        if (attention_mask is None and keys.shape[-2] == Lq and q.is_cuda
+                and q.dtype in (torch.float16, torch.bfloat16)):
+            lat = keys if keys.dim() == 3 else keys.transpose(1, 2).reshape(B, Lq, -1)
+            k_full = prefill.rebuild_keys(lat, self.k_u_heads(), self.k_ranks(), cos, sin)
+            v_full = prefill.rebuild_values(values, self.v_proj.U.weight, Hkv)
+            return prefill.prompt_attention(q, k_full, v_full, self.scaling)
         if keys.dim() == 4:                                                    # (B, Hkv, L, r)
             u = torch.stack(self.k_u_heads()).to(keys.dtype)                   # (Hkv, D, r)
             k_full = torch.matmul(keys, u.transpose(-2, -1))                   # (B, Hkv, L, D)

@@ -354,3 +354,35 @@ def read_device_error(ws: Optional[torch.Tensor] = None, device="cuda") -> int:
     code = C.c_int(0)
     check(load().starkv_read_device_error(_ptr(ws), C.byref(code), _stream()), "starkv_read_device_error")
     return int(code.value)
+
+
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scaling: float,
+                      out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                      error_word: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal prompt attention (``starkv_prefill_attention``): q (B, Hq, T, 128),
+    k / v (B, Hkv, T, 128), fp16 or bf16, any strides whose channel dimension is
+    contiguous (e.g. ``x.view(B, T, H, 128).transpose(1, 2)``).  Returns (B, Hq, T, 128)
+    in ``out_dtype`` (default: q's dtype), or writes ``out`` (any such strides)."""
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    if D != 128 or k.shape != (B, Hkv, T, 128) or v.shape != (B, Hkv, T, 128):
+        raise _lib.StarKVError("prefill_attention: q (B, Hq, T, 128), k / v (B, Hkv, T, 128)")
+    if k.dtype != q.dtype or v.dtype != q.dtype:
+        raise _lib.StarKVError("prefill_attention: q, k and v must share one dtype")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.stride(3) != 1:
+            raise _lib.StarKVError(f"prefill_attention: {name} channels must be contiguous")
+    if out is None:
+        out = torch.empty(B, Hq, T, 128, dtype=out_dtype or q.dtype, device=q.device)
+    elif out.shape != (B, Hq, T, 128) or out.stride(3) != 1:
+        raise _lib.StarKVError("prefill_attention: out must be (B, Hq, T, 128) with contiguous channels")
+    a = _lib.PrefillArgs()
+    a.q, a.k, a.v, a.out = _ptr(q), _ptr(k), _ptr(v), _ptr(out)
+    for dst, t in ((a.q_strides, q), (a.k_strides, k), (a.v_strides, v), (a.out_strides, out)):
+        dst[0], dst[1], dst[2] = t.stride(0), t.stride(1), t.stride(2)
+    a.dtype, a.out_dtype = dtype_code(q.dtype), dtype_code(out.dtype)
+    a.batch, a.num_q_heads, a.num_kv_heads, a.num_tokens = B, Hq, Hkv, T
+    a.scaling = float(scaling)
+    a.error_word = _ptr(error_word)
+    check(load().starkv_prefill_attention(C.byref(a), _stream()), "starkv_prefill_attention")
+    return out
