@@ -10,14 +10,18 @@
 //
 // Roles (256 threads, one CTA per SM: it holds all 512 TMEM columns):
 //   * warps 0-3 (thread = query row): softmax.  S_j = Q K_j^T lands in TMEM
-//     (fp32, 128 columns, two buffers); the row maximum and exp2 weights are
-//     formed in two passes over S_j, P_j is written back to TMEM as the 16-bit A
-//     operand (64 columns, two buffers), and the previous tile's P V result is
-//     folded into the fp32 output row kept in registers (o = o * alpha + pv).
-//   * warp 4, one thread: tcgen05.mma issue.  S_{j+1} is issued before waiting
-//     for P_j so that the tensor core computes the next logits while the
-//     softmax warps work; P_j V_j goes into one 128-column accumulator.
-//   * warps 5-7: cp.async staging of the Q tile and of a two-stage ring of
+//     (fp32, 128 columns, two buffers) and is read once into registers; P_j =
+//     exp2(S_j * scale - m) goes back to TMEM as the 16-bit A operand (64
+//     columns, two buffers).  The output O accumulates in TMEM across tiles
+//     (P_j V_j with accumulate).  The running maximum m of a row moves only when
+//     a tile's maximum exceeds it by more than 2^8 (so every weight stays <= 256,
+//     exact in fp16 / bf16 range): then the row's O and l are scaled by
+//     exp2(m_old - m_new) in place, after P_{j-1} V_{j-1} has completed.  Most
+//     rows rescale in their first few tiles only.
+//   * warp 4 lane 0 issues S_j = Q K_j^T (8 tcgen05.mma, M = N = 128, K = 16);
+//     warp 5 lane 0 issues O += P_j V_j (A = P_j from TMEM, V_j MN-major).  Two
+//     issuing threads keep the tensor core at its rate for N = 128.
+//   * warps 6-7: cp.async staging of the Q tile and of a three-stage ring of
 //     (K_j, V_j) tiles, 16-byte chunks written straight into the canonical
 //     no-swizzle layouts (K and Q K-major, V MN-major: no transposition).
 // Every mbarrier wait is bounded; a wait that runs out records an error code,
@@ -37,9 +41,10 @@ constexpr int kPfThreads = 256;
 constexpr int kPfTile = 128;                    // queries per CTA and keys per step
 constexpr int kPfTileBytes = 128 * 128 * 2;     // one 128 x 128 16-bit tile
 constexpr int kPfHeader = 1024;                 // barriers + TMEM address + abort flag
-constexpr size_t kPfSmem = kPfHeader + 5 * (size_t)kPfTileBytes;   // Q + 2 x (K, V)
+constexpr int kPfStages = 3;                    // (K, V) tile ring
+constexpr size_t kPfSmem = kPfHeader + (1 + 2 * kPfStages) * (size_t)kPfTileBytes;   // Q + ring
 
-// TMEM columns: S buffers, the P V accumulator and the P buffers (16-bit pairs).
+// TMEM columns: S buffers, the output accumulator and the P buffers (16-bit pairs).
 constexpr uint32_t kPfColS = 0, kPfColO = 256, kPfColP = 384;
 
 struct PrefillParams {
@@ -123,17 +128,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
   uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;     // [2]
-  uint64_t* kv_empty = bar + 3;    // [2]
-  uint64_t* s_full = bar + 5;      // [2]
-  uint64_t* p_full = bar + 7;      // [2]
-  uint64_t* o_full = bar + 9;
-  uint64_t* o_free = bar + 10;
-  uint64_t* mma_done = bar + 11;
+  uint64_t* kv_full = bar + 1;     // [3]
+  uint64_t* kv_empty = bar + 4;    // [3]
+  uint64_t* s_full = bar + 7;      // [2]
+  uint64_t* p_full = bar + 9;      // [2]
+  uint64_t* o_done = bar + 11;     // [2]: P_j V_j complete, j mod 2
+  uint64_t* s_done = bar + 13;     // S issuer's MMAs complete (teardown)
+  uint64_t* pv_done = bar + 14;    // P V issuer's MMAs complete (teardown)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 256);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 260);
   uint8_t* Qs = smem + kPfHeader;
-  uint8_t* KVs = Qs + kPfTileBytes;    // stage s: K at 2*s, V at 2*s+1 tiles
+  uint8_t* KVs = Qs + kPfTileBytes;    // stage s: K tile at 2*s, V tile at 2*s+1
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int per = p.num_q_heads * p.batch;
@@ -146,16 +151,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
   const unsigned long long lim = p.wait_ns;
 
   if (tid == 0) {
-    mbar_init(q_full, 96);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(kv_full + s, 96);
+    mbar_init(q_full, 64);
+    for (int s = 0; s < kPfStages; ++s) {
+      mbar_init(kv_full + s, 64);
       mbar_init(kv_empty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(s_full + s, 1);
       mbar_init(p_full + s, 128);
+      mbar_init(o_done + s, 1);
     }
-    mbar_init(o_full, 1);
-    mbar_init(o_free, 128);
-    mbar_init(mma_done, 1);
+    mbar_init(s_done, 1);
+    mbar_init(pv_done, 1);
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -176,9 +183,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
     return false;
   };
 
-  if (warp >= 5) {
+  if (warp >= 6) {
     // ---------------------------------------------------------------- producer
-    const int pt = tid - 160;
+    const int pt = tid - 192;
     const uint8_t* qsrc = reinterpret_cast<const uint8_t*>(p.q) +
                           2 * (b * p.q_stride[0] + h * p.q_stride[1]);
     const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(p.k) +
@@ -186,76 +193,70 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
     const uint8_t* vsrc = reinterpret_cast<const uint8_t*>(p.v) +
                           2 * (b * p.v_stride[0] + kvh * p.v_stride[1]);
     const int64_t qrs = 2 * p.q_stride[2], krs = 2 * p.k_stride[2], vrs = 2 * p.v_stride[2];
-    pf_stage_tile<false>(Qs, qsrc, qrs, qt * kPfTile, p.num_tokens, pt, 96);
+    pf_stage_tile<false>(Qs, qsrc, qrs, qt * kPfTile, p.num_tokens, pt, 64);
     cp_async_commit();
     auto issue = [&](int j) {
-      uint8_t* st = KVs + (size_t)(j & 1) * 2 * kPfTileBytes;
-      pf_stage_tile<false>(st, ksrc, krs, j * kPfTile, p.num_tokens, pt, 96);
-      pf_stage_tile<true>(st + kPfTileBytes, vsrc, vrs, j * kPfTile, p.num_tokens, pt, 96);
+      uint8_t* st = KVs + (size_t)(j % kPfStages) * 2 * kPfTileBytes;
+      pf_stage_tile<false>(st, ksrc, krs, j * kPfTile, p.num_tokens, pt, 64);
+      pf_stage_tile<true>(st + kPfTileBytes, vsrc, vrs, j * kPfTile, p.num_tokens, pt, 64);
       cp_async_commit();
     };
-    // Tile j is announced before the producer waits to refill a stage with tile
-    // j+1: the MMA thread needs tile j (for S_j) before it issues P_{j-1} V_{j-1},
-    // the MMAs whose completion frees that stage.
+    // Tile j is announced as soon as its copies land; tile j+2 then goes into the
+    // stage of tile j-1 once P_{j-1} V_{j-1} has read it.  Two tiles stay in flight.
     issue(0);
-    if (n > 1) {
-      issue(1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    fence_proxy_async_smem();
-    mbar_arrive(q_full);
-    mbar_arrive(kv_full);
-    for (int j = 1; j < n; ++j) {
-      cp_async_wait<0>();
+    if (n > 1) issue(1);
+    for (int j = 0; j < n; ++j) {
+      if (j + 1 < n) cp_async_wait<1>(); else cp_async_wait<0>();
       fence_proxy_async_smem();
-      mbar_arrive(kv_full + (j & 1));
-      if (j + 1 < n) {
-        if (!wait(kv_empty + ((j + 1) & 1), (((j + 1) >> 1) - 1) & 1, kDevWaitMma)) break;
-        issue(j + 1);
+      if (j == 0) mbar_arrive(q_full);
+      mbar_arrive(kv_full + (j % kPfStages));
+      if (j + 2 < n) {
+        if (j >= 1 && !wait(kv_empty + ((j + 2) % kPfStages), ((j - 1) / kPfStages) & 1, kDevWaitMma)) break;
+        issue(j + 2);
       }
     }
     cp_async_wait<0>();
   } else if (warp == 4) {
-    // ------------------------------------------------------------- MMA issue
+    // ------------------------------------------------------------ S = Q K^T
     if (lane == 0) {
-      constexpr uint32_t IS = idesc_pf<T>(false), IO = idesc_pf<T>(true);
+      constexpr uint32_t IS = idesc_pf<T>(false);
       const uint32_t qa = smem_u32(Qs);
-      auto issue_s = [&](int j) {
-        const uint32_t kb = smem_u32(KVs + (size_t)(j & 1) * 2 * kPfTileBytes);
+      bool ok = wait(q_full, 0, kDevWaitCopy);
+      for (int j = 0; ok && j < n; ++j) {
+        if (!wait(kv_full + (j % kPfStages), (j / kPfStages) & 1, kDevWaitCopy)) break;
+        // S buffer j mod 2 was read by the softmax for tile j-2
+        if (j >= 2 && !wait(p_full + (j & 1), ((j - 2) >> 1) & 1, kDevWaitMma)) break;
+        tc_fence_after();
+        const uint32_t kb = smem_u32(KVs + (size_t)(j % kPfStages) * 2 * kPfTileBytes);
         const uint32_t d = tmem + kPfColS + (uint32_t)(j & 1) * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           mma_f16_ss(d, smem_desc(qa + kk * 256, 128, 2048), smem_desc(kb + kk * 256, 128, 2048), IS,
                      kk > 0 ? 1u : 0u);
         mma_commit(s_full + (j & 1));
-      };
-      bool ok = wait(q_full, 0, kDevWaitCopy) && wait(kv_full, 0, kDevWaitCopy);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
       }
-      for (int j = 0; ok && j < n; ++j) {
-        if (j + 1 < n) {
-          if (!wait(kv_full + ((j + 1) & 1), ((j + 1) >> 1) & 1, kDevWaitCopy)) break;
-          tc_fence_after();
-          issue_s(j + 1);
-        }
+      mma_commit(s_done);
+      mbar_wait(s_done, 0, lim);
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ O += P V
+    if (lane == 0) {
+      constexpr uint32_t IO = idesc_pf<T>(true);
+      for (int j = 0; j < n; ++j) {
         if (!wait(p_full + (j & 1), (j >> 1) & 1, kDevWaitMma)) break;
-        if (j >= 1 && !wait(o_free, (j - 1) & 1, kDevWaitMma)) break;
         tc_fence_after();
-        const uint32_t vb = smem_u32(KVs + (size_t)(j & 1) * 2 * kPfTileBytes + kPfTileBytes);
+        const uint32_t vb = smem_u32(KVs + (size_t)(j % kPfStages) * 2 * kPfTileBytes + kPfTileBytes);
         const uint32_t pa = tmem + kPfColP + (uint32_t)(j & 1) * 64;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ts(tmem + kPfColO, pa + kk * 8, smem_desc(vb + kk * 256, 128, 2048), IO, kk > 0 ? 1u : 0u);
-        mma_commit(o_full);
-        mma_commit(kv_empty + (j & 1));
+          mma_f16_ts(tmem + kPfColO, pa + kk * 8, smem_desc(vb + kk * 256, 128, 2048), IO,
+                     (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(o_done + (j & 1));
+        mma_commit(kv_empty + (j % kPfStages));
       }
-      // every issued MMA has finished before TMEM is released
-      mma_commit(mma_done);
-      mbar_wait(mma_done, 0, lim);
+      mma_commit(pv_done);
+      mbar_wait(pv_done, 0, lim);
     }
     __syncwarp();
   } else {
@@ -263,95 +264,112 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
     const int row = tid;                             // TMEM lane == query row
     const int qpos = qt * kPfTile + row;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    float o[128];
-#pragma unroll
-    for (int i = 0; i < 128; ++i) o[i] = 0.f;
-    float m_run = kNegBig, l_run = 0.f, alpha_prev = 0.f;
+    const uint32_t o_col = tmem + lane_base + kPfColO;
+    float m_run = kNegBig, l_run = 0.f;
     const float sl2 = p.scale_log2;
+    constexpr float kLazy = 8.f;                     // log2 of the largest weight
     bool ok = true;
-    auto fold = [&](int j) -> bool {                 // o = o * alpha_j + (P_j V_j)
-      if (!__all_sync(0xffffffffu, wait(o_full, j & 1, kDevWaitMma))) return false;
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float v[16];
-        tmem_ld16(tmem + lane_base + kPfColO + c * 16, v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[c * 16 + i] = fmaf(o[c * 16 + i], alpha_prev, v[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(o_free);
-      return true;
-    };
     for (int j = 0; j < n; ++j) {
       if (!__all_sync(0xffffffffu, wait(s_full + (j & 1), (j >> 1) & 1, kDevWaitMma))) { ok = false; break; }
       tc_fence_after();
       const uint32_t sa = tmem + lane_base + kPfColS + (uint32_t)(j & 1) * 128;
-      const bool diag = (j == qt);
-      const int kmax = diag ? row : 127;               // last kept key column of this row
+      float sv[128];
+      tmem_ld32x2(sa, sa + 32, sv, sv + 32);
+      tmem_ld32x2(sa + 64, sa + 96, sv + 64, sv + 96);
+      const int kmax = (j == qt) ? row : 127;          // last kept key column of this row
       float mx = kNegBig;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float v[16];
-        tmem_ld16(sa + c * 16, v);
+      for (int i = 0; i < 128; ++i) mx = (i <= kmax) ? fmaxf(mx, sv[i]) : mx;
+      const float mt = mx * sl2;
+      if (j == 0) {
+        m_run = mt;
+      } else {
+        const bool need = mt > m_run + kLazy;
+        float alpha = 1.f;
+        if (need) {
+          alpha = fast_exp2(m_run - mt);
+          m_run = mt;
+          l_run *= alpha;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          // O holds P_0 V_0 + ... + P_{j-1} V_{j-1} once P_{j-1} V_{j-1} completes
+          if (!__all_sync(0xffffffffu, wait(o_done + ((j - 1) & 1), ((j - 1) >> 1) & 1, kDevWaitMma))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) mx = (c * 16 + i <= kmax) ? fmaxf(mx, v[i]) : mx;
+          for (int c = 0; c < 8; ++c) {
+            float v[16];
+            tmem_ld16(o_col + c * 16, v);
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(v[i] * alpha);
+            tmem_st16(o_col + c * 16, w);
+          }
+        }
       }
-      const float m_new = fmaxf(m_run, mx * sl2);
-      const float alpha = fast_exp2(m_run - m_new);
+      // P buffer j mod 2 was read by P_{j-2} V_{j-2}
+      if (j >= 2 && !__all_sync(0xffffffffu, wait(o_done + (j & 1), ((j - 2) >> 1) & 1, kDevWaitMma))) {
+        ok = false;
+        break;
+      }
       float lsum = 0.f;
       const uint32_t pcol = tmem + lane_base + kPfColP + (uint32_t)(j & 1) * 64;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        float v[16];
-        tmem_ld16(sa + c * 16, v);
-        uint32_t pk[8];
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; i += 2) {
-          const float p0 = (c * 16 + i <= kmax) ? fast_exp2(fmaf(v[i], sl2, -m_new)) : 0.f;
-          const float p1 = (c * 16 + i + 1 <= kmax) ? fast_exp2(fmaf(v[i + 1], sl2, -m_new)) : 0.f;
+        for (int i = 0; i < 32; i += 2) {
+          const int col = c * 32 + i;
+          const float p0 = (col <= kmax) ? fast_exp2(fmaf(sv[col], sl2, -m_run)) : 0.f;
+          const float p1 = (col + 1 <= kmax) ? fast_exp2(fmaf(sv[col + 1], sl2, -m_run)) : 0.f;
           lsum += p0 + p1;
           pk[i >> 1] = pack2<T>(p0, p1);
         }
-        tmem_st8(pcol + c * 8, pk);
+        tmem_st16(pcol + c * 16, pk);
       }
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full + (j & 1));
-      l_run = fmaf(l_run, alpha, lsum);
-      m_run = m_new;
-      if (j >= 1 && !fold(j - 1)) { ok = false; break; }
-      alpha_prev = alpha;
+      l_run += lsum;
     }
-    if (ok && n >= 1) ok = fold(n - 1);
-    if (ok && qpos < p.num_tokens) {
+    if (ok) ok = __all_sync(0xffffffffu, wait(o_done + ((n - 1) & 1), ((n - 1) >> 1) & 1, kDevWaitMma));
+    if (ok) {
+      tc_fence_after();
       const float inv = 1.f / l_run;
-#pragma unroll
-      for (int i = 0; i < 128; ++i) o[i] *= inv;
+      const bool live = qpos < p.num_tokens;
       uint8_t* dst = reinterpret_cast<uint8_t*>(p.out);
       const int64_t base = b * p.o_stride[0] + h * p.o_stride[1] + (int64_t)qpos * p.o_stride[2];
-      if (p.out_dtype == STARKV_F32) {
-        float4* d4 = reinterpret_cast<float4*>(dst + 4 * base);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          d4[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-      } else {
-        uint4* d4 = reinterpret_cast<uint4*>(dst + 2 * base);
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tmem_ld16(o_col + c * 16, v);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          uint4 w;
-          if (p.out_dtype == STARKV_BF16) {
-            w.x = pack2<__nv_bfloat16>(o[8 * i], o[8 * i + 1]);
-            w.y = pack2<__nv_bfloat16>(o[8 * i + 2], o[8 * i + 3]);
-            w.z = pack2<__nv_bfloat16>(o[8 * i + 4], o[8 * i + 5]);
-            w.w = pack2<__nv_bfloat16>(o[8 * i + 6], o[8 * i + 7]);
-          } else {
-            w.x = pack2<__half>(o[8 * i], o[8 * i + 1]);
-            w.y = pack2<__half>(o[8 * i + 2], o[8 * i + 3]);
-            w.z = pack2<__half>(o[8 * i + 4], o[8 * i + 5]);
-            w.w = pack2<__half>(o[8 * i + 6], o[8 * i + 7]);
+        for (int i = 0; i < 16; ++i) v[i] *= inv;
+        if (!live) continue;
+        if (p.out_dtype == STARKV_F32) {
+          float4* d4 = reinterpret_cast<float4*>(dst + 4 * (base + c * 16));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 2 * (base + c * 16));
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            uint4 w;
+            if (p.out_dtype == STARKV_BF16) {
+              w.x = pack2<__nv_bfloat16>(v[8 * i], v[8 * i + 1]);
+              w.y = pack2<__nv_bfloat16>(v[8 * i + 2], v[8 * i + 3]);
+              w.z = pack2<__nv_bfloat16>(v[8 * i + 4], v[8 * i + 5]);
+              w.w = pack2<__nv_bfloat16>(v[8 * i + 6], v[8 * i + 7]);
+            } else {
+              w.x = pack2<__half>(v[8 * i], v[8 * i + 1]);
+              w.y = pack2<__half>(v[8 * i + 2], v[8 * i + 3]);
+              w.z = pack2<__half>(v[8 * i + 4], v[8 * i + 5]);
+              w.w = pack2<__half>(v[8 * i + 6], v[8 * i + 7]);
+            }
+            d4[i] = w;
           }
-          d4[i] = w;
         }
       }
     }
