@@ -8,24 +8,30 @@
 // head (GQA by index), q / k / v / out as strided (B, H, T, 128) views so that
 // the projections' (B, T, H, 128) tensors are read and written in place.
 //
-// Roles (256 threads, one CTA per SM: it holds all 512 TMEM columns):
-//   * warps 0-3 (thread = query row): softmax.  S_j = Q K_j^T lands in TMEM
-//     (fp32, 128 columns, two buffers) and is read once into registers; P_j =
-//     exp2(S_j * scale - m) goes back to TMEM as the 16-bit A operand (64
-//     columns, two buffers).  The output O accumulates in TMEM across tiles
-//     (P_j V_j with accumulate).  The running maximum m of a row moves only when
-//     a tile's maximum exceeds it by more than 2^8 (so every weight stays <= 256,
-//     exact in fp16 / bf16 range): then the row's O and l are scaled by
-//     exp2(m_old - m_new) in place, after P_{j-1} V_{j-1} has completed.  Most
-//     rows rescale in their first few tiles only.
-//   * warp 4 lane 0 issues S_j = Q K_j^T (8 tcgen05.mma, M = N = 128, K = 16);
-//     warp 5 lane 0 issues O += P_j V_j (A = P_j from TMEM, V_j MN-major).  Two
+// Roles (384 threads, one CTA per SM: it holds all 512 TMEM columns and 227 KB
+// of shared memory):
+//   * warps 0-7: softmax.  Query row r is shared by thread r (key columns 0-63
+//     of every tile) and thread 128 + r (columns 64-127), both on TMEM lane r.
+//     S_j = Q K_j^T lands in TMEM (fp32, 128 columns, two buffers) and each
+//     thread reads its 64 columns once; the two halves of a row trade their
+//     maxima (and, at the end, their sums) through shared memory under an
+//     mbarrier.  P_j = exp2(S_j * scale - m) goes back to TMEM as the 16-bit A
+//     operand (64 columns, two buffers); one weight in four is a degree-3
+//     polynomial on the FMA pipe instead of MUFU ex2, which paces the rest.  The
+//     output O accumulates in TMEM across tiles (P_j V_j with accumulate).  The
+//     running maximum m of a row moves only when a tile's maximum exceeds it by
+//     more than 2^8 (every weight stays <= 256): then the row's O and l are
+//     scaled by exp2(m_old - m_new) in place, after P_{j-1} V_{j-1} has
+//     completed.  Most rows rescale in their first few tiles only.
+//   * warp 8 lane 0 issues S_j = Q K_j^T (8 tcgen05.mma, M = N = 128, K = 16);
+//     warp 9 lane 0 issues O += P_j V_j (A = P_j from TMEM, V_j MN-major).  Two
 //     issuing threads keep the tensor core at its rate for N = 128.
-//   * warps 6-7: cp.async staging of the Q tile and of a three-stage ring of
+//   * warps 10-11: cp.async staging of the Q tile and of a three-stage ring of
 //     (K_j, V_j) tiles, 16-byte chunks written straight into the canonical
 //     no-swizzle layouts (K and Q K-major, V MN-major: no transposition).
-// Every mbarrier wait is bounded; a wait that runs out records an error code,
-// sets the CTA's abort flag and the roles leave their loops.
+// Every wait is bounded (mbarriers only, no named barriers); a wait that runs
+// out records an error code, sets the CTA's abort flag and the roles leave
+// their loops.
 #pragma once
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -37,10 +43,10 @@
 
 namespace starkv {
 
-constexpr int kPfThreads = 256;
+constexpr int kPfThreads = 384;
 constexpr int kPfTile = 128;                    // queries per CTA and keys per step
 constexpr int kPfTileBytes = 128 * 128 * 2;     // one 128 x 128 16-bit tile
-constexpr int kPfHeader = 1024;                 // barriers + TMEM address + abort flag
+constexpr int kPfHeader = 3072;                 // barriers, TMEM address, abort flag, row exchange
 constexpr int kPfStages = 3;                    // (K, V) tile ring
 constexpr size_t kPfSmem = kPfHeader + (1 + 2 * kPfStages) * (size_t)kPfTileBytes;   // Q + ring
 
@@ -76,6 +82,21 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x for x <= 8 on the FMA pipe: 2^x = 2^floor(x) * 2^f, f in [0, 1), with
+// 2^f ~ 1 + f (c1 + f (c2 + f c3)) (coefficients fitted here by least squares on
+// the relative error over [0, 1): |rel err| <= 8.7e-5, below half an ulp of fp16).
+// The exponent is added to the bit pattern; x is clamped at -126 (the result
+// there is ~1e-38, 0 after rounding to fp16).
+__device__ __forceinline__ float poly_exp2(float x) {
+  x = fmaxf(x, -126.f);
+  const float fl = floorf(x);
+  const float f = x - fl;
+  float r = fmaf(f, 0.07705805f, 0.22764558f);
+  r = fmaf(f, r, 0.69512290f);
+  r = fmaf(f, r, 1.0f);
+  return __int_as_float(__float_as_int(r) + (static_cast<int>(fl) << 23));
 }
 
 // 16-byte cp.async that reads src_bytes (0 or 16) and zero-fills the rest.
@@ -135,6 +156,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
   uint64_t* o_done = bar + 11;     // [2]: P_j V_j complete, j mod 2
   uint64_t* s_done = bar + 13;     // S issuer's MMAs complete (teardown)
   uint64_t* pv_done = bar + 14;    // P V issuer's MMAs complete (teardown)
+  uint64_t* xchg = bar + 15;       // [2]: both halves of every row wrote their partial, j mod 2
+  float* red = reinterpret_cast<float*>(smem + 1024);   // [2][2][128] row partials
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 256);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 260);
   uint8_t* Qs = smem + kPfHeader;
@@ -158,15 +181,16 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(s_full + s, 1);
-      mbar_init(p_full + s, 128);
+      mbar_init(p_full + s, 256);
       mbar_init(o_done + s, 1);
+      mbar_init(xchg + s, 256);
     }
     mbar_init(s_done, 1);
     mbar_init(pv_done, 1);
     *s_abort = 0;
     fence_mbar_init();
   }
-  if (warp == 4) {
+  if (warp == 8) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -183,9 +207,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
     return false;
   };
 
-  if (warp >= 6) {
+  if (warp >= 10) {
     // ---------------------------------------------------------------- producer
-    const int pt = tid - 192;
+    const int pt = tid - 320;
     const uint8_t* qsrc = reinterpret_cast<const uint8_t*>(p.q) +
                           2 * (b * p.q_stride[0] + h * p.q_stride[1]);
     const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(p.k) +
@@ -216,7 +240,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
       }
     }
     cp_async_wait<0>();
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------------------ S = Q K^T
     if (lane == 0) {
       constexpr uint32_t IS = idesc_pf<T>(false);
@@ -239,7 +263,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
       mbar_wait(s_done, 0, lim);
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ O += P V
     if (lane == 0) {
       constexpr uint32_t IO = idesc_pf<T>(true);
@@ -261,26 +285,35 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
     __syncwarp();
   } else {
     // ---------------------------------------------------------------- softmax
-    const int row = tid;                             // TMEM lane == query row
+    const int row = tid & 127, half = tid >> 7;     // TMEM lane == query row
     const int qpos = qt * kPfTile + row;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const uint32_t o_col = tmem + lane_base + kPfColO;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t o_col = tmem + lane_base + kPfColO + half * 64;
     float m_run = kNegBig, l_run = 0.f;
     const float sl2 = p.scale_log2;
     constexpr float kLazy = 8.f;                     // log2 of the largest weight
+    // trade a per-row partial with the other half of the row (slot k mod 2)
+    auto trade = [&](int k, float v) -> float {
+      float* r = red + (k & 1) * 256;
+      r[half * 128 + row] = v;
+      mbar_arrive(xchg + (k & 1));
+      if (!wait(xchg + (k & 1), (k >> 1) & 1, kDevWaitMma)) return NAN;
+      return r[(half ^ 1) * 128 + row];
+    };
     bool ok = true;
     for (int j = 0; j < n; ++j) {
       if (!__all_sync(0xffffffffu, wait(s_full + (j & 1), (j >> 1) & 1, kDevWaitMma))) { ok = false; break; }
       tc_fence_after();
-      const uint32_t sa = tmem + lane_base + kPfColS + (uint32_t)(j & 1) * 128;
-      float sv[128];
+      const uint32_t sa = tmem + lane_base + kPfColS + (uint32_t)(j & 1) * 128 + half * 64;
+      float sv[64];
       tmem_ld32x2(sa, sa + 32, sv, sv + 32);
-      tmem_ld32x2(sa + 64, sa + 96, sv + 64, sv + 96);
-      const int kmax = (j == qt) ? row : 127;          // last kept key column of this row
-      float mx = kNegBig;
+      const int kmax = (j == qt) ? row - half * 64 : 63;   // last kept column of this half (may be < 0)
+      float mq[4] = {kNegBig, kNegBig, kNegBig, kNegBig};
 #pragma unroll
-      for (int i = 0; i < 128; ++i) mx = (i <= kmax) ? fmaxf(mx, sv[i]) : mx;
-      const float mt = mx * sl2;
+      for (int i = 0; i < 64; ++i) mq[i & 3] = (i <= kmax) ? fmaxf(mq[i & 3], sv[i]) : mq[i & 3];
+      const float other = trade(j, fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])));
+      if (!__all_sync(0xffffffffu, !isnan(other))) { ok = false; break; }
+      const float mt = fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])), other) * sl2;
       if (j == 0) {
         m_run = mt;
       } else {
@@ -299,7 +332,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
           }
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
+          for (int c = 0; c < 4; ++c) {
             float v[16];
             tmem_ld16(o_col + c * 16, v);
             uint32_t w[16];
@@ -314,17 +347,20 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
         ok = false;
         break;
       }
-      float lsum = 0.f;
-      const uint32_t pcol = tmem + lane_base + kPfColP + (uint32_t)(j & 1) * 64;
+      float ls0 = 0.f, ls1 = 0.f;
+      const uint32_t pcol = tmem + lane_base + kPfColP + (uint32_t)(j & 1) * 64 + half * 32;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
           const int col = c * 32 + i;
-          const float p0 = (col <= kmax) ? fast_exp2(fmaf(sv[col], sl2, -m_run)) : 0.f;
-          const float p1 = (col + 1 <= kmax) ? fast_exp2(fmaf(sv[col + 1], sl2, -m_run)) : 0.f;
-          lsum += p0 + p1;
+          const float x0 = fmaf(sv[col], sl2, -m_run), x1 = fmaf(sv[col + 1], sl2, -m_run);
+          const float e1 = ((col & 3) == 2) ? poly_exp2(x1) : fast_exp2(x1);
+          const float p0 = (col <= kmax) ? fast_exp2(x0) : 0.f;
+          const float p1 = (col + 1 <= kmax) ? e1 : 0.f;
+          ls0 += p0;
+          ls1 += p1;
           pk[i >> 1] = pack2<T>(p0, p1);
         }
         tmem_st16(pcol + c * 16, pk);
@@ -332,17 +368,23 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full + (j & 1));
-      l_run += lsum;
+      l_run += ls0 + ls1;
     }
     if (ok) ok = __all_sync(0xffffffffu, wait(o_done + ((n - 1) & 1), ((n - 1) >> 1) & 1, kDevWaitMma));
+    float l_tot = 0.f;
+    if (ok) {
+      const float other = trade(n, l_run);
+      ok = __all_sync(0xffffffffu, !isnan(other));
+      l_tot = l_run + other;
+    }
     if (ok) {
       tc_fence_after();
-      const float inv = 1.f / l_run;
+      const float inv = 1.f / l_tot;
       const bool live = qpos < p.num_tokens;
       uint8_t* dst = reinterpret_cast<uint8_t*>(p.out);
-      const int64_t base = b * p.o_stride[0] + h * p.o_stride[1] + (int64_t)qpos * p.o_stride[2];
+      const int64_t base = b * p.o_stride[0] + h * p.o_stride[1] + (int64_t)qpos * p.o_stride[2] + half * 64;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 4; ++c) {
         float v[16];
         tmem_ld16(o_col + c * 16, v);
 #pragma unroll
@@ -376,7 +418,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
