@@ -8,7 +8,7 @@
 // head (GQA by index), q / k / v / out as strided (B, H, T, 128) views so that
 // the projections' (B, T, H, 128) tensors are read and written in place.
 //
-// Roles (384 threads, one CTA per SM: it holds all 512 TMEM columns and 227 KB
+// Roles (352 threads, one CTA per SM: it holds all 512 TMEM columns and 227 KB
 // of shared memory):
 //   * warps 0-7: softmax.  Query row r is shared by thread r (key columns 0-63
 //     of every tile) and thread 128 + r (columns 64-127), both on TMEM lane r.
@@ -26,13 +26,16 @@
 //   * warp 8 lane 0 issues S_j = Q K_j^T (8 tcgen05.mma, M = N = 128, K = 16);
 //     warp 9 lane 0 issues O += P_j V_j (A = P_j from TMEM, V_j MN-major).  Two
 //     issuing threads keep the tensor core at its rate for N = 128.
-//   * warps 10-11: cp.async staging of the Q tile and of a three-stage ring of
-//     (K_j, V_j) tiles, 16-byte chunks written straight into the canonical
-//     no-swizzle layouts (K and Q K-major, V MN-major: no transposition).
+//   * warp 10 lane 0: TMA loads of the Q tile and of a three-stage ring of
+//     (K_j, V_j) tiles, each tile two 64-channel x 128-row boxes in the 128-byte
+//     swizzled layout, which is the canonical K-major layout for Q and K and the
+//     MN-major one for V (channels along N, tokens along K: no transposition).
+//     Rows past the sequence end are filled with zeros by the TMA unit.
 // Every wait is bounded (mbarriers only, no named barriers); a wait that runs
 // out records an error code, sets the CTA's abort flag and the roles leave
 // their loops.
 #pragma once
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -43,7 +46,7 @@
 
 namespace starkv {
 
-constexpr int kPfThreads = 384;
+constexpr int kPfThreads = 352;
 constexpr int kPfTile = 128;                    // queries per CTA and keys per step
 constexpr int kPfTileBytes = 128 * 128 * 2;     // one 128 x 128 16-bit tile
 constexpr int kPfHeader = 3072;                 // barriers, TMEM address, abort flag, row exchange
@@ -67,7 +70,18 @@ struct PrefillParams {
   float scale_log2;        // softmax scale * log2(e)
   int* err;                // device error word (nullable)
   unsigned long long wait_ns;
+  long long* trace;        // diagnostic builds (STARKV_PFTRACE): CTA 0 timeline, else null
+  uint32_t v_lbo, v_sbo;   // V operand descriptor strides (MN-major, 128-byte swizzle)
 };
+
+#ifdef STARKV_PFTRACE
+#define PFTRACE(j, f)                                                                           \
+  do {                                                                                          \
+    if (p.trace && blockIdx.x == 0 && (j) < 512) p.trace[(j) * 16 + (f)] = clock64();            \
+  } while (0)
+#else
+#define PFTRACE(j, f) do { } while (0)
+#endif
 
 // Instruction descriptor, kind::f16 with A = B = 16-bit type T, D = f32, A K-major,
 // B K-major (b_mn = false) or MN-major (b_mn = true), M = N = 128.
@@ -99,11 +113,21 @@ __device__ __forceinline__ float poly_exp2(float x) {
   return __int_as_float(__float_as_int(r) + (static_cast<int>(fl) << 23));
 }
 
-// 16-byte cp.async that reads src_bytes (0 or 16) and zero-fills the rest.
-__device__ __forceinline__ void cp_async16_zfill(void* dst_smem, const void* src_gmem, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst_smem)), "l"(src_gmem),
-               "r"(src_bytes)
-               : "memory");
+// Shared-memory matrix descriptor for the 128-byte swizzled canonical layouts
+// (rows of 128 bytes, 16-byte chunks XOR-ed with row % 8, 8-row atoms of 1024
+// bytes at 1024-byte aligned addresses).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return smem_desc(saddr, lbo, sbo) | (2ull << 61);
+}
+
+// 4-D tiled TMA load (no multicast) completing on `bar` as transaction bytes.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
 }
 
 template <typename T>
@@ -119,33 +143,10 @@ __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Stage one 128-row tile (rows [row0, row0+128) of a strided (T, 128) matrix,
-// rows >= T zero) into the canonical no-swizzle layout.  Chunk c (16 bytes) of
-// the tile lands at byte 16*c.  K-major (Q, K: row = M/N index, 8 channels per
-// chunk): row = c%8 + 8*(c/128), channel block = (c/8)%16.  MN-major (V: the 8
-// channels of a chunk run along N, the token along K): token = c%8 + 8*((c/8)%16),
-// channel block = c/128.
-template <bool MN>
-__device__ __forceinline__ void pf_stage_tile(uint8_t* dst, const uint8_t* src, int64_t row_stride_bytes,
-                                              int row0, int T, int tid, int nthreads) {
-  for (int c = tid; c < 2048; c += nthreads) {
-    int row, blk;
-    if (MN) {
-      row = (c & 7) + 8 * ((c >> 3) & 15);
-      blk = c >> 7;
-    } else {
-      row = (c & 7) + 8 * (c >> 7);
-      blk = (c >> 3) & 15;
-    }
-    const int gr = row0 + row;
-    const bool ok = gr < T;
-    const uint8_t* s = src + (int64_t)(ok ? gr : 0) * row_stride_bytes + blk * 16;
-    cp_async16_zfill(dst + 16 * c, s, ok ? 16u : 0u);
-  }
-}
-
 template <typename T>
-__global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const PrefillParams p) {
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_attn_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
+                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
   uint64_t* q_full = bar + 0;
@@ -174,9 +175,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
   const unsigned long long lim = p.wait_ns;
 
   if (tid == 0) {
-    mbar_init(q_full, 64);
+    mbar_init(q_full, 1);
     for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(kv_full + s, 64);
+      mbar_init(kv_full + s, 1);
       mbar_init(kv_empty + s, 1);
     }
     for (int s = 0; s < 2; ++s) {
@@ -207,39 +208,28 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
     return false;
   };
 
-  if (warp >= 10) {
+  if (warp == 10) {
     // ---------------------------------------------------------------- producer
-    const int pt = tid - 320;
-    const uint8_t* qsrc = reinterpret_cast<const uint8_t*>(p.q) +
-                          2 * (b * p.q_stride[0] + h * p.q_stride[1]);
-    const uint8_t* ksrc = reinterpret_cast<const uint8_t*>(p.k) +
-                          2 * (b * p.k_stride[0] + kvh * p.k_stride[1]);
-    const uint8_t* vsrc = reinterpret_cast<const uint8_t*>(p.v) +
-                          2 * (b * p.v_stride[0] + kvh * p.v_stride[1]);
-    const int64_t qrs = 2 * p.q_stride[2], krs = 2 * p.k_stride[2], vrs = 2 * p.v_stride[2];
-    pf_stage_tile<false>(Qs, qsrc, qrs, qt * kPfTile, p.num_tokens, pt, 64);
-    cp_async_commit();
-    auto issue = [&](int j) {
-      uint8_t* st = KVs + (size_t)(j % kPfStages) * 2 * kPfTileBytes;
-      pf_stage_tile<false>(st, ksrc, krs, j * kPfTile, p.num_tokens, pt, 64);
-      pf_stage_tile<true>(st + kPfTileBytes, vsrc, vrs, j * kPfTile, p.num_tokens, pt, 64);
-      cp_async_commit();
-    };
-    // Tile j is announced as soon as its copies land; tile j+2 then goes into the
-    // stage of tile j-1 once P_{j-1} V_{j-1} has read it.  Two tiles stay in flight.
-    issue(0);
-    if (n > 1) issue(1);
-    for (int j = 0; j < n; ++j) {
-      if (j + 1 < n) cp_async_wait<1>(); else cp_async_wait<0>();
-      fence_proxy_async_smem();
-      if (j == 0) mbar_arrive(q_full);
-      mbar_arrive(kv_full + (j % kPfStages));
-      if (j + 2 < n) {
-        if (j >= 1 && !wait(kv_empty + ((j + 2) % kPfStages), ((j - 1) / kPfStages) & 1, kDevWaitMma)) break;
-        issue(j + 2);
+    if (lane == 0) {
+      // a tile is two 64-channel boxes of 128 rows (128-byte swizzle), 16 KB each
+      mbar_arrive_expect_tx(q_full, kPfTileBytes);
+      tma_load_4d(Qs, &tm_q, 0, qt * kPfTile, h, b, q_full);
+      tma_load_4d(Qs + kPfTileBytes / 2, &tm_q, 64, qt * kPfTile, h, b, q_full);
+      for (int j = 0; j < n; ++j) {
+        const int st = j % kPfStages;
+        if (j >= kPfStages && !wait(kv_empty + st, ((j / kPfStages) - 1) & 1, kDevWaitMma)) break;
+        if (j >= kPfStages) PFTRACE(j, 1);
+        uint8_t* kt = KVs + (size_t)st * 2 * kPfTileBytes;
+        uint8_t* vt = kt + kPfTileBytes;
+        mbar_arrive_expect_tx(kv_full + st, 2 * kPfTileBytes);
+        tma_load_4d(kt, &tm_k, 0, j * kPfTile, kvh, b, kv_full + st);
+        tma_load_4d(kt + kPfTileBytes / 2, &tm_k, 64, j * kPfTile, kvh, b, kv_full + st);
+        tma_load_4d(vt, &tm_v, 0, j * kPfTile, kvh, b, kv_full + st);
+        tma_load_4d(vt + kPfTileBytes / 2, &tm_v, 64, j * kPfTile, kvh, b, kv_full + st);
+        PFTRACE(j, 2);
       }
     }
-    cp_async_wait<0>();
+    __syncwarp();
   } else if (warp == 8) {
     // ------------------------------------------------------------ S = Q K^T
     if (lane == 0) {
@@ -249,15 +239,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
       for (int j = 0; ok && j < n; ++j) {
         if (!wait(kv_full + (j % kPfStages), (j / kPfStages) & 1, kDevWaitCopy)) break;
         // S buffer j mod 2 was read by the softmax for tile j-2
+        PFTRACE(j, 3);                             // tile j present
         if (j >= 2 && !wait(p_full + (j & 1), ((j - 2) >> 1) & 1, kDevWaitMma)) break;
+        PFTRACE(j, 4);                             // S buffer free
         tc_fence_after();
         const uint32_t kb = smem_u32(KVs + (size_t)(j % kPfStages) * 2 * kPfTileBytes);
         const uint32_t d = tmem + kPfColS + (uint32_t)(j & 1) * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ss(d, smem_desc(qa + kk * 256, 128, 2048), smem_desc(kb + kk * 256, 128, 2048), IS,
+          mma_f16_ss(d, smem_desc_sw128(qa + (kk >> 2) * (kPfTileBytes / 2) + (kk & 3) * 32, 16, 1024),
+                     smem_desc_sw128(kb + (kk >> 2) * (kPfTileBytes / 2) + (kk & 3) * 32, 16, 1024), IS,
                      kk > 0 ? 1u : 0u);
         mma_commit(s_full + (j & 1));
+        PFTRACE(j, 5);                             // S_j issued
       }
       mma_commit(s_done);
       mbar_wait(s_done, 0, lim);
@@ -269,15 +263,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
       constexpr uint32_t IO = idesc_pf<T>(true);
       for (int j = 0; j < n; ++j) {
         if (!wait(p_full + (j & 1), (j >> 1) & 1, kDevWaitMma)) break;
+        PFTRACE(j, 6);                             // P_j ready
         tc_fence_after();
         const uint32_t vb = smem_u32(KVs + (size_t)(j % kPfStages) * 2 * kPfTileBytes + kPfTileBytes);
         const uint32_t pa = tmem + kPfColP + (uint32_t)(j & 1) * 64;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ts(tmem + kPfColO, pa + kk * 8, smem_desc(vb + kk * 256, 128, 2048), IO,
+          mma_f16_ts(tmem + kPfColO, pa + kk * 8, smem_desc_sw128(vb + kk * 2048, p.v_lbo, p.v_sbo), IO,
                      (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(o_done + (j & 1));
         mma_commit(kv_empty + (j % kPfStages));
+        PFTRACE(j, 7);                             // P_j V_j issued
       }
       mma_commit(pv_done);
       mbar_wait(pv_done, 0, lim);
@@ -303,6 +299,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
     bool ok = true;
     for (int j = 0; j < n; ++j) {
       if (!__all_sync(0xffffffffu, wait(s_full + (j & 1), (j >> 1) & 1, kDevWaitMma))) { ok = false; break; }
+      if (tid == 0) PFTRACE(j, 8);                 // S_j complete
       tc_fence_after();
       const uint32_t sa = tmem + lane_base + kPfColS + (uint32_t)(j & 1) * 128 + half * 64;
       float sv[64];
@@ -311,7 +308,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
       float mq[4] = {kNegBig, kNegBig, kNegBig, kNegBig};
 #pragma unroll
       for (int i = 0; i < 64; ++i) mq[i & 3] = (i <= kmax) ? fmaxf(mq[i & 3], sv[i]) : mq[i & 3];
+      if (tid == 0) PFTRACE(j, 9);                 // S_j loaded, local max
       const float other = trade(j, fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])));
+      if (tid == 0) PFTRACE(j, 10);                // row maxima traded
       if (!__all_sync(0xffffffffu, !isnan(other))) { ok = false; break; }
       const float mt = fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])), other) * sl2;
       if (j == 0) {
@@ -347,6 +346,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
         ok = false;
         break;
       }
+      if (tid == 0) PFTRACE(j, 11);                // rescale done, P buffer free
       float ls0 = 0.f, ls1 = 0.f;
       const uint32_t pcol = tmem + lane_base + kPfColP + (uint32_t)(j & 1) * 64 + half * 32;
 #pragma unroll
@@ -368,6 +368,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_kernel(const Prefi
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full + (j & 1));
+      if (tid == 0) PFTRACE(j, 12);                // P_j written
       l_run += ls0 + ls1;
     }
     if (ok) ok = __all_sync(0xffffffffu, wait(o_done + ((n - 1) & 1), ((n - 1) >> 1) & 1, kDevWaitMma));

@@ -1,9 +1,11 @@
 // starkv_abi.cu — the extern "C" entry points of libstarkv.so (declared in
 // include/starkv.h): validation, launch geometry, workspace carving and the
 // kernel launches of the decode step.  No entry point allocates device memory.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <type_traits>
 
@@ -25,6 +27,9 @@ unsigned long long g_wait_ns = kWaitLimitNs;
 int g_skip_unit = -1;
 #ifdef STARKV_KTRACE
 long long* g_ktrace = nullptr;   // diagnostic builds only
+#endif
+#ifdef STARKV_PFTRACE
+long long* g_pftrace = nullptr;  // diagnostic builds only
 #endif
 
 int fail_launch() {
@@ -59,7 +64,7 @@ int device_sm_count(int* dev_out) {
 // Raise a kernel's dynamic shared-memory limit once per (kernel, device).
 template <typename K>
 int ensure_smem(K kernel, size_t bytes, int slot) {
-  constexpr int kSlots = 24;
+  constexpr int kSlots = 28;
   static size_t configured[kSlots][kMaxDevices] = {{0}};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -295,6 +300,42 @@ int validate(const starkv_layout* lp) {
   if (vcol != l.v_rank_total) return set_error(STARKV_ERR_INVALID, "v_rank_total mismatch");
   if (k_geometry(l).G == 0) return set_error(STARKV_ERR_UNSUPPORTED, "K ranks too large for shared memory");
   if (l.num_q_heads / k_geometry(l).G > kKMaxGroups) return set_error(STARKV_ERR_UNSUPPORTED, "more than 64 K head groups");
+  return STARKV_OK;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (the library
+// links only the CUDA runtime).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    fn = reinterpret_cast<EncodeTiledFn>(f);
+  }
+  return fn;
+}
+
+// Tensor map of a strided (B, H, T, 128) 16-bit tensor: boxes of 64 channels x
+// 128 tokens of one (head, sequence), 128-byte swizzle, zero fill past T.
+int prefill_map(CUtensorMap* map, const void* base, int dtype, int B, int H, int T, const int64_t* strides) {
+  EncodeTiledFn enc = encode_tiled();
+  if (!enc) return set_error(STARKV_ERR_LAUNCH, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[4] = {128, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t gstr[3] = {(cuuint64_t)strides[2] * 2, (cuuint64_t)strides[1] * 2, (cuuint64_t)strides[0] * 2};
+  const cuuint32_t box[4] = {64, 128, 1, 1};
+  const cuuint32_t es[4] = {1, 1, 1, 1};
+  const CUresult r = enc(map, dtype == STARKV_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         4, const_cast<void*>(base), dims, gstr, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(STARKV_ERR_INVALID, "cuTensorMapEncodeTiled rejected a prefill tensor");
   return STARKV_OK;
 }
 
@@ -761,6 +802,15 @@ extern "C" int starkv_debug_ktrace(void* buf) {
 }
 #endif
 
+#ifdef STARKV_PFTRACE
+// Diagnostic builds only: prefill kernel timeline of CTA 0 (16 stamps per key
+// tile, 512 tiles at most), or null to stop.
+extern "C" int starkv_debug_pftrace(void* buf) {
+  g_pftrace = reinterpret_cast<long long*>(buf);
+  return STARKV_OK;
+}
+#endif
+
 int starkv_set_test_hooks(int64_t wait_limit_ns, int32_t skip_copy_unit) {
   g_wait_ns = wait_limit_ns > 0 ? (unsigned long long)wait_limit_ns : kWaitLimitNs;
   g_skip_unit = skip_copy_unit;
@@ -908,17 +958,35 @@ int starkv_prefill_attention(const starkv_prefill_args* a, starkv_stream_t strea
   p.scale_log2 = a->scaling * 1.4426950408889634f;
   p.err = a->error_word;
   p.wait_ns = g_wait_ns;
+#ifdef STARKV_PFTRACE
+  p.trace = g_pftrace;
+#endif
+  // V operand descriptor (MN-major, 128-byte swizzle): the second 64-channel box
+  // sits 16 KB along N, 8-token groups 1 KB apart along K
+  p.v_lbo = 16384;
+  p.v_sbo = 1024;
+#ifdef STARKV_PFTRACE
+  if (getenv("STARKV_PF_VSWAP")) {
+    p.v_lbo = 1024;
+    p.v_sbo = 16384;
+  }
+#endif
+  CUtensorMap tq, tk, tv;
+  if ((rc = prefill_map(&tq, a->q, a->dtype, a->batch, a->num_q_heads, a->num_tokens, a->q_strides)) ||
+      (rc = prefill_map(&tk, a->k, a->dtype, a->batch, a->num_kv_heads, a->num_tokens, a->k_strides)) ||
+      (rc = prefill_map(&tv, a->v, a->dtype, a->batch, a->num_kv_heads, a->num_tokens, a->v_strides)))
+    return rc;
   const int64_t ctas = (int64_t)p.n_qtiles * a->num_q_heads * a->batch;
   if (ctas > 0x7fffffff) return set_error(STARKV_ERR_UNSUPPORTED, "too many query tiles");
   cudaStream_t st = (cudaStream_t)stream;
   if (a->dtype == STARKV_F16) {
-    rc = ensure_smem(prefill_attn_kernel<__half>, kPfSmem, 20);
+    rc = ensure_smem(prefill_attn_kernel<__half>, kPfSmem, 24);
     if (rc) return rc;
-    prefill_attn_kernel<__half><<<(unsigned)ctas, kPfThreads, kPfSmem, st>>>(p);
+    prefill_attn_kernel<__half><<<(unsigned)ctas, kPfThreads, kPfSmem, st>>>(p, tq, tk, tv);
   } else {
-    rc = ensure_smem(prefill_attn_kernel<__nv_bfloat16>, kPfSmem, 21);
+    rc = ensure_smem(prefill_attn_kernel<__nv_bfloat16>, kPfSmem, 25);
     if (rc) return rc;
-    prefill_attn_kernel<__nv_bfloat16><<<(unsigned)ctas, kPfThreads, kPfSmem, st>>>(p);
+    prefill_attn_kernel<__nv_bfloat16><<<(unsigned)ctas, kPfThreads, kPfSmem, st>>>(p, tq, tk, tv);
   }
   return fail_launch();
 }
