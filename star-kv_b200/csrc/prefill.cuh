@@ -12,17 +12,17 @@
 // of shared memory):
 //   * warps 0-7: softmax.  Query row r is shared by thread r (key columns 0-63
 //     of every tile) and thread 128 + r (columns 64-127), both on TMEM lane r.
-//     S_j = Q K_j^T lands in TMEM (fp32, 128 columns, two buffers) and each
-//     thread reads its 64 columns once; the two halves of a row trade their
-//     maxima (and, at the end, their sums) through shared memory under an
-//     mbarrier.  P_j = exp2(S_j * scale - m) goes back to TMEM as the 16-bit A
-//     operand (64 columns, two buffers); one weight in four is a degree-3
-//     polynomial on the FMA pipe instead of MUFU ex2, which paces the rest.  The
-//     output O accumulates in TMEM across tiles (P_j V_j with accumulate).  The
-//     running maximum m of a row moves only when a tile's maximum exceeds it by
-//     more than 2^8 (every weight stays <= 256): then the row's O and l are
-//     scaled by exp2(m_old - m_new) in place, after P_{j-1} V_{j-1} has
-//     completed.  Most rows rescale in their first few tiles only.
+//     S_j = Q K_j^T lands in TMEM (fp32, 128 columns, two buffers); both
+//     threads of a row read the whole row, so each forms the row maximum itself,
+//     and each writes the weights of its own 64 keys: x = S * scale - m in
+//     fp32, rounded to fp16 pairs, 2^x by one packed MUFU ex2 per pair (the
+//     fp16 results are P_j itself, or are rounded to bf16), back to TMEM as the
+//     16-bit A operand (64 columns, two buffers).  The output O accumulates in
+//     TMEM across tiles (P_j V_j with accumulate).  The running maximum m of a
+//     row moves only when a tile's maximum exceeds it by more than 2^2 (so x <= 2,
+//     where fp16 holds x to 2^-10): then the row's O and l are scaled by
+//     exp2(m_old - m_new) in place, after P_{j-1} V_{j-1} has completed.  The
+//     two halves' sums l meet once, at the end, through shared memory.
 //   * warp 8 lane 0 issues S_j = Q K_j^T (8 tcgen05.mma, M = N = 128, K = 16);
 //     warp 9 lane 0 issues O += P_j V_j (A = P_j from TMEM, V_j MN-major).  Two
 //     issuing threads keep the tensor core at its rate for N = 128.
@@ -98,19 +98,16 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// 2^x for x <= 8 on the FMA pipe: 2^x = 2^floor(x) * 2^f, f in [0, 1), with
-// 2^f ~ 1 + f (c1 + f (c2 + f c3)) (coefficients fitted here by least squares on
-// the relative error over [0, 1): |rel err| <= 8.7e-5, below half an ulp of fp16).
-// The exponent is added to the bit pattern; x is clamped at -126 (the result
-// there is ~1e-38, 0 after rounding to fp16).
-__device__ __forceinline__ float poly_exp2(float x) {
-  x = fmaxf(x, -126.f);
-  const float fl = floorf(x);
-  const float f = x - fl;
-  float r = fmaf(f, 0.07705805f, 0.22764558f);
-  r = fmaf(f, r, 0.69512290f);
-  r = fmaf(f, r, 1.0f);
-  return __int_as_float(__float_as_int(r) + (static_cast<int>(fl) << 23));
+// Packed 2^x of two fp16 values (one MUFU instruction for both).
+__device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
 }
 
 // Shared-memory matrix descriptor for the 128-byte swizzled canonical layouts
@@ -287,8 +284,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const uint32_t o_col = tmem + lane_base + kPfColO + half * 64;
     float m_run = kNegBig, l_run = 0.f;
     const float sl2 = p.scale_log2;
-    constexpr float kLazy = 8.f;                     // log2 of the largest weight
-    // trade a per-row partial with the other half of the row (slot k mod 2)
+    constexpr float kLazy = 2.f;                     // log2 of the largest weight (fp16 ex2 input precision)
+    // trade a per-row partial with the other half of the row (slot k mod 2, phase k / 2)
     auto trade = [&](int k, float v) -> float {
       float* r = red + (k & 1) * 256;
       r[half * 128 + row] = v;
@@ -301,18 +298,32 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       if (!__all_sync(0xffffffffu, wait(s_full + (j & 1), (j >> 1) & 1, kDevWaitMma))) { ok = false; break; }
       if (tid == 0) PFTRACE(j, 8);                 // S_j complete
       tc_fence_after();
-      const uint32_t sa = tmem + lane_base + kPfColS + (uint32_t)(j & 1) * 128 + half * 64;
-      float sv[64];
-      tmem_ld32x2(sa, sa + 32, sv, sv + 32);
-      const int kmax = (j == qt) ? row - half * 64 : 63;   // last kept column of this half (may be < 0)
+      // both threads of a row read the whole row: the row maximum needs no exchange
+      const uint32_t sa = tmem + lane_base + kPfColS + (uint32_t)(j & 1) * 128;
+      float sv[64], so[64];                            // own half, other half
+      tmem_ld32x2(sa + half * 64, sa + half * 64 + 32, sv, sv + 32);
+      tmem_ld32x2(sa + (half ^ 1) * 64, sa + (half ^ 1) * 64 + 32, so, so + 32);
+      const bool diag = (j == qt);
+      const int kmax = diag ? row - half * 64 : 63;            // last kept column of the own half
+      const int kmax_o = diag ? row - (half ^ 1) * 64 : 63;    // ... of the other half
       float mq[4] = {kNegBig, kNegBig, kNegBig, kNegBig};
+      if (!diag) {                                     // no masking off the diagonal
 #pragma unroll
-      for (int i = 0; i < 64; ++i) mq[i & 3] = (i <= kmax) ? fmaxf(mq[i & 3], sv[i]) : mq[i & 3];
-      if (tid == 0) PFTRACE(j, 9);                 // S_j loaded, local max
-      const float other = trade(j, fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])));
-      if (tid == 0) PFTRACE(j, 10);                // row maxima traded
-      if (!__all_sync(0xffffffffu, !isnan(other))) { ok = false; break; }
-      const float mt = fmaxf(fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])), other) * sl2;
+        for (int i = 0; i < 64; i += 2) {
+          mq[0] = fmaxf(mq[0], sv[i]);
+          mq[1] = fmaxf(mq[1], sv[i + 1]);
+          mq[2] = fmaxf(mq[2], so[i]);
+          mq[3] = fmaxf(mq[3], so[i + 1]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          mq[i & 1] = (i <= kmax) ? fmaxf(mq[i & 1], sv[i]) : mq[i & 1];
+          mq[2 + (i & 1)] = (i <= kmax_o) ? fmaxf(mq[2 + (i & 1)], so[i]) : mq[2 + (i & 1)];
+        }
+      }
+      if (tid == 0) PFTRACE(j, 9);                 // S_j loaded, row max
+      const float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
       if (j == 0) {
         m_run = mt;
       } else {
@@ -347,34 +358,51 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         break;
       }
       if (tid == 0) PFTRACE(j, 11);                // rescale done, P buffer free
-      float ls0 = 0.f, ls1 = 0.f;
+      // weights: x = s * scale - m in fp32 (x <= kLazy), rounded to fp16 pairs,
+      // one packed MUFU ex2 per pair; masked keys get x = -inf (weight 0)
+      __half2 acc[4] = {__float2half2_rn(0.f), __float2half2_rn(0.f), __float2half2_rn(0.f),
+                        __float2half2_rn(0.f)};
       const uint32_t pcol = tmem + lane_base + kPfColP + (uint32_t)(j & 1) * 64 + half * 32;
+      auto weights = [&](auto masked) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16];
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const int col = c * 32 + i;
-          const float x0 = fmaf(sv[col], sl2, -m_run), x1 = fmaf(sv[col + 1], sl2, -m_run);
-          const float e1 = ((col & 3) == 2) ? poly_exp2(x1) : fast_exp2(x1);
-          const float p0 = (col <= kmax) ? fast_exp2(x0) : 0.f;
-          const float p1 = (col + 1 <= kmax) ? e1 : 0.f;
-          ls0 += p0;
-          ls1 += p1;
-          pk[i >> 1] = pack2<T>(p0, p1);
+          for (int i = 0; i < 16; ++i) {
+            const int col = c * 32 + 2 * i;
+            float x0 = fmaf(sv[col], sl2, -m_run), x1 = fmaf(sv[col + 1], sl2, -m_run);
+            if constexpr (decltype(masked)::value) {
+              x0 = (col <= kmax) ? x0 : -INFINITY;
+              x1 = (col + 1 <= kmax) ? x1 : -INFINITY;
+            }
+            const uint32_t e = ex2_h2(f2_to_h2(x0, x1));
+            acc[i & 3] = __hadd2(acc[i & 3], *reinterpret_cast<const __half2*>(&e));
+            if constexpr (std::is_same<T, __half>::value) {
+              pk[i] = e;
+            } else {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&e));
+              pk[i] = pack2<__nv_bfloat16>(f.x, f.y);
+            }
+          }
+          tmem_st16(pcol + c * 16, pk);
         }
-        tmem_st16(pcol + c * 16, pk);
-      }
+      };
+      if (diag)
+        weights(std::true_type());
+      else
+        weights(std::false_type());
+      const float2 s01 = __half22float2(__hadd2(acc[0], acc[1]));
+      const float2 s23 = __half22float2(__hadd2(acc[2], acc[3]));
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(p_full + (j & 1));
       if (tid == 0) PFTRACE(j, 12);                // P_j written
-      l_run += ls0 + ls1;
+      l_run += (s01.x + s01.y) + (s23.x + s23.y);
     }
     if (ok) ok = __all_sync(0xffffffffu, wait(o_done + ((n - 1) & 1), ((n - 1) >> 1) & 1, kDevWaitMma));
     float l_tot = 0.f;
     if (ok) {
-      const float other = trade(n, l_run);
+      const float other = trade(0, l_run);
       ok = __all_sync(0xffffffffu, !isnan(other));
       l_tot = l_run + other;
     }
