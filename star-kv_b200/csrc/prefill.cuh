@@ -15,8 +15,10 @@
 //     S_j = Q K_j^T lands in TMEM (fp32, 128 columns, two buffers); both
 //     threads of a row read the whole row, so each forms the row maximum itself,
 //     and each writes the weights of its own 64 keys: x = S * scale - m in
-//     fp32, rounded to fp16 pairs, 2^x by one packed MUFU ex2 per pair (the
-//     fp16 results are P_j itself, or are rounded to bf16), back to TMEM as the
+//     fp32, 2^x by a packed MUFU ex2 of the fp16-rounded pair for half of the
+//     pairs and by a packed fp32x2 polynomial on the FMA pipe for the other
+//     half (MUFU alone paces the tile otherwise); the fp16 results are P_j
+//     itself, or are rounded to bf16, and go back to TMEM as the
 //     16-bit A operand (64 columns, two buffers).  The output O accumulates in
 //     TMEM across tiles (P_j V_j with accumulate).  The running maximum m of a
 //     row moves only when a tile's maximum exceeds it by more than 2^2 (so x <= 2,
@@ -103,6 +105,26 @@ __device__ __forceinline__ uint32_t ex2_h2(uint32_t x) {
   uint32_t y;
   asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
   return y;
+}
+
+// 2^x of two fp32 values on the FMA pipe (packed fp32x2 arithmetic), for x <= 2:
+// n = round(x) through the 1.5 * 2^23 rounding constant, f = x - n in [-0.5, 0.5],
+// 2^f ~ 1 + f (c1 + f (c2 + f c3)) (coefficients fitted here to the relative
+// error on [-0.5, 0.5]: |rel err| <= 1.02e-4, below half an ulp of fp16), and n
+// added to the exponent field.  x is clamped at -127 (the result is then below
+// the fp16 range and rounds to 0).
+__device__ __forceinline__ float2 poly_exp2x2(float2 x) {
+  constexpr float kRound = 12582912.f;             // 1.5 * 2^23, bit pattern 0x4B400000
+  x = make_float2(fmaxf(x.x, -127.f), fmaxf(x.y, -127.f));
+  const float2 r = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(r, make_float2(-kRound, -kRound));
+  const float2 f = __fadd2_rn(x, make_float2(-n.x, -n.y));
+  float2 q = __ffma2_rn(f, make_float2(0.05500900f, 0.05500900f), make_float2(0.24221100f, 0.24221100f));
+  q = __ffma2_rn(f, q, make_float2(0.69328290f, 0.69328290f));
+  q = __ffma2_rn(f, q, make_float2(1.f, 1.f));
+  const uint32_t ex = (uint32_t)(__float_as_int(r.x) - 0x4B400000) << 23;
+  const uint32_t ey = (uint32_t)(__float_as_int(r.y) - 0x4B400000) << 23;
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + ex), __uint_as_float(__float_as_uint(q.y) + ey));
 }
 
 __device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
@@ -375,7 +397,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
               x0 = (col <= kmax) ? x0 : -INFINITY;
               x1 = (col + 1 <= kmax) ? x1 : -INFINITY;
             }
-            const uint32_t e = ex2_h2(f2_to_h2(x0, x1));
+            // half of the pairs on MUFU (packed fp16 ex2), half on the FMA pipe
+            uint32_t e;
+            if (i & 1) {
+              const float2 y = poly_exp2x2(make_float2(x0, x1));
+              e = f2_to_h2(y.x, y.y);
+            } else {
+              e = ex2_h2(f2_to_h2(x0, x1));
+            }
             acc[i & 3] = __hadd2(acc[i & 3], *reinterpret_cast<const __half2*>(&e));
             if constexpr (std::is_same<T, __half>::value) {
               pk[i] = e;

@@ -5,7 +5,6 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
-#include <cstdlib>
 #include <cstring>
 #include <type_traits>
 
@@ -965,12 +964,6 @@ int starkv_prefill_attention(const starkv_prefill_args* a, starkv_stream_t strea
   // sits 16 KB along N, 8-token groups 1 KB apart along K
   p.v_lbo = 16384;
   p.v_sbo = 1024;
-#ifdef STARKV_PFTRACE
-  if (getenv("STARKV_PF_VSWAP")) {
-    p.v_lbo = 1024;
-    p.v_sbo = 16384;
-  }
-#endif
   CUtensorMap tq, tk, tv;
   if ((rc = prefill_map(&tq, a->q, a->dtype, a->batch, a->num_q_heads, a->num_tokens, a->q_strides)) ||
       (rc = prefill_map(&tk, a->k, a->dtype, a->batch, a->num_kv_heads, a->num_tokens, a->k_strides)) ||
