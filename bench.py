@@ -183,7 +183,8 @@ def run_c3(args):
     prompt = torch.randint(0, model.config.vocab_size, (1, ctx), generator=g, device="cuda")
     generate(model, prompt[:, :64], 4)                       # warm-up: kernels, workspaces
     t0 = time.perf_counter()
-    ids, per_tok = generate(model, prompt, 128)
+    st = {}
+    ids, per_tok = generate(model, prompt, 128, stats=st)
     wall = time.perf_counter() - t0
     print(json.dumps({
         "metric": "end-to-end greedy decode tokens/s (c3)", "value": 1.0 / per_tok, "unit": "tokens/s",
@@ -191,7 +192,7 @@ def run_c3(args):
         "data": "synthetic (random-init weights, random prompt)", "vs_baseline": None,
         "config": {"workload": "c3: 32-layer Llama-2-7B-shaped model, STAR-KV int8 K / int4 V attention per "
                                "layer, batch 1, 128 new tokens", "context": ctx, "new_tokens": 128},
-        "prompt_plus_decode_wall_s": wall}), flush=True)
+        "prompt_ms": st["prompt_s"] * 1e3, "prompt_plus_decode_wall_s": wall}), flush=True)
 
 
 # ---------------------------------------------------------------- GPU arm

@@ -8,8 +8,8 @@ drawn from a seed (default average K rank 32 of {16, 32, 48}, V blocks of 4 KV
 heads with ranks in {64, 128, 192}), K heads ragged (``starkv.export``).
 
 The prompt goes through the modules' prompt path (latents stored in the
-``StarKVCache``, attention with SDPA on the reconstructed keys/values, as the
-reference's prefill does, model.py:429-449); every generated token goes through
+``StarKVCache``, keys/values rebuilt from the latents as the reference's prefill
+does, model.py:429-449, causal attention by the library's tcgen05 prefill kernel); every generated token goes through
 the fused decode path per layer: ``starkv_project_append`` (latent projection +
 quantise-append) and ``starkv_decode_attention``.  The rest of each layer (norms,
 MLP, embeddings, LM head) is the transformers Llama code.
@@ -24,7 +24,7 @@ from __future__ import annotations
 import argparse
 import json
 import time
-from typing import List, Sequence
+from typing import List, Optional, Sequence
 
 import numpy as np
 import torch
@@ -91,11 +91,15 @@ def forward_tokens(model, ids: torch.Tensor, start: int, cache: StarKVCache) -> 
 
 
 @torch.no_grad()
-def generate(model, prompt: torch.Tensor, new_tokens: int, capacity: int = 0):
-    """Greedy decode: returns (generated ids (B, new_tokens), decode seconds per token)."""
+def generate(model, prompt: torch.Tensor, new_tokens: int, capacity: int = 0, stats: Optional[dict] = None):
+    """Greedy decode: returns (generated ids (B, new_tokens), decode seconds per token).
+    ``stats`` (optional dict) receives ``prompt_s``: device time of the prompt pass."""
     B, P = prompt.shape
     cache = StarKVCache(capacity or P + new_tokens, quantized=getattr(model, "starkv_quantized", True))
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
     logits = forward_tokens(model, prompt, 0, cache)
+    p1.record()
     tok = logits.argmax(-1, keepdim=True)
     out: List[torch.Tensor] = [tok]
     torch.cuda.synchronize()
@@ -108,6 +112,8 @@ def generate(model, prompt: torch.Tensor, new_tokens: int, capacity: int = 0):
     e1.record()
     torch.cuda.synchronize()
     per_tok = e0.elapsed_time(e1) / 1e3 / max(1, new_tokens - 1)
+    if stats is not None:
+        stats["prompt_s"] = p0.elapsed_time(p1) / 1e3
     return torch.cat(out, dim=1), per_tok
 
 
@@ -125,9 +131,10 @@ def main():
     g = torch.Generator(device="cuda").manual_seed(a.seed + 1)
     prompt = torch.randint(0, model.config.vocab_size, (a.batch, a.context), generator=g, device="cuda")
     generate(model, prompt[:, :16], 4)                      # warm-up (kernels, workspaces)
-    ids, per_tok = generate(model, prompt, a.new)
+    st = {}
+    ids, per_tok = generate(model, prompt, a.new, stats=st)
     print(json.dumps({"metric": "end-to-end greedy decode (c3)", "value": a.batch / per_tok, "unit": "tokens/s",
-                      "ms_per_token": per_tok * 1e3, "batch": a.batch, "context": a.context, "new_tokens": a.new,
+                      "ms_per_token": per_tok * 1e3, "prompt_ms": st["prompt_s"] * 1e3, "batch": a.batch, "context": a.context, "new_tokens": a.new,
                       "layers": a.layers, "quantized": not a.unquantized, "weights": "random-init fp16",
                       "first_tokens": ids[0, :8].tolist(), "wall_s": time.time() - t0}))
 

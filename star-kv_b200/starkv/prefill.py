@@ -26,7 +26,7 @@ def rebuild_keys(k_lat: torch.Tensor, k_u_heads: Sequence[torch.Tensor], k_ranks
     out = torch.empty(B, len(k_ranks), T, 128, dtype=k_lat.dtype, device=k_lat.device)
     c0 = 0
     for h, (r, u) in enumerate(zip(k_ranks, k_u_heads)):
-        torch.matmul(k_lat[..., c0:c0 + r], u.to(k_lat.dtype).T, out=out[:, h])
+        out[:, h] = torch.matmul(k_lat[..., c0:c0 + r], u.to(k_lat.dtype).T)
         c0 += r
     half = 64
     rot = torch.cat([-out[..., half:], out[..., :half]], dim=-1)
