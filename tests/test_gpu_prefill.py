@@ -38,7 +38,7 @@ def _rel(a, b):
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("B,Hq,Hkv,T", [(2, 8, 2, 300), (1, 4, 4, 128), (1, 2, 1, 1), (1, 2, 2, 129),
-                                        (3, 6, 3, 517)])
+                                        (3, 6, 3, 517), (1, 2, 1, 16384)])
 def test_prefill_kernel_matches_fp32_attention(cuda, dtype, B, Hq, Hkv, T):
     g = torch.Generator(device=cuda).manual_seed(B * 1000 + T)
     # (B, T, H, 128) projections read through transposed views, as the module passes them
