@@ -482,4 +482,314 @@ __global__ void __launch_bounds__(kPfThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Two query tiles per CTA.  CTA = (pair of 128-query tiles 2i, 2i+1, query
+// head, sequence): both tiles share every K / V tile load and the tensor core
+// alternates between them.  TMEM: tile X in {0, 1} owns columns 256X..256X+255
+// — S_j (fp32, 128 columns) at +0, overwritten by P_j (16-bit pairs, 64
+// columns) once its row has been read, and the output accumulator at +128.
+// One thread issues every MMA, so they execute in issue order: S_X(j+1) is
+// issued after P_X(j) V_j and may overwrite the P_X(j) it reads, and the commit
+// that announces S_X(j+1) also covers P_X(j) V_j (the softmax may then rescale
+// O_X and write P_X(j+1)).  Warps 0-3 own tile 0, warps 4-7 tile 1, one thread
+// per query row holding the whole S row: no cross-thread exchange.
+constexpr int kPf2Threads = 320;
+constexpr int kPf2Stages = 2;
+constexpr size_t kPf2Smem = kPfHeader + (2 + 2 * kPf2Stages) * (size_t)kPfTileBytes;
+
+template <typename T>
+__global__ void __launch_bounds__(kPf2Threads, 1)
+    prefill_attn2_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
+                         const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* q_full = bar + 0;
+  uint64_t* kv_full = bar + 1;     // [2]
+  uint64_t* kv_empty = bar + 3;    // [2]
+  uint64_t* s_full = bar + 5;      // [2]: per query tile
+  uint64_t* p_full = bar + 7;      // [2]: per query tile
+  uint64_t* o_done = bar + 9;      // [2]: per query tile, last P V complete
+  uint64_t* mma_done = bar + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 256);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 260);
+  uint8_t* Qs = smem + kPfHeader;                  // tile X at X * kPfTileBytes
+  uint8_t* KVs = Qs + 2 * kPfTileBytes;            // stage s: K at 2s, V at 2s+1
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int per = p.num_q_heads * p.batch;
+  const int npairs = (p.n_qtiles + 1) >> 1;
+  const int pi = npairs - 1 - (int)blockIdx.x / per;   // heaviest pairs first
+  const int h = ((int)blockIdx.x % per) % p.num_q_heads;
+  const int b = ((int)blockIdx.x % per) / p.num_q_heads;
+  const int kvh = h / (p.num_q_heads / p.num_kv_heads);
+  const int q0 = 2 * pi;                           // query tiles q0, q0 + 1
+  const bool has1 = q0 + 1 < p.n_qtiles;
+  const int n0 = q0 + 1;                           // key tiles of query tile 0
+  const int nk = has1 ? q0 + 2 : n0;               // key tiles the CTA loads
+  const unsigned long long lim = p.wait_ns;
+
+  if (tid == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(kv_full + s, 1);
+      mbar_init(kv_empty + s, 1);
+      mbar_init(s_full + s, 1);
+      mbar_init(p_full + s, 128);
+      mbar_init(o_done + s, 1);
+    }
+    mbar_init(mma_done, 1);
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto wait = [&](uint64_t* bar_, uint32_t parity, int code) -> bool {
+    if (*s_abort) return false;
+    if (mbar_wait(bar_, parity, lim)) return true;
+    record_error(p.err, code);
+    *s_abort = 1;
+    return false;
+  };
+
+  if (warp == 9) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, (has1 ? 2 : 1) * kPfTileBytes);
+      for (int x = 0; x < (has1 ? 2 : 1); ++x) {
+        tma_load_4d(Qs + x * kPfTileBytes, &tm_q, 0, (q0 + x) * kPfTile, h, b, q_full);
+        tma_load_4d(Qs + x * kPfTileBytes + kPfTileBytes / 2, &tm_q, 64, (q0 + x) * kPfTile, h, b, q_full);
+      }
+      for (int j = 0; j < nk; ++j) {
+        const int st = j % kPf2Stages;
+        if (j >= kPf2Stages && !wait(kv_empty + st, ((j / kPf2Stages) - 1) & 1, kDevWaitMma)) break;
+        uint8_t* kt = KVs + (size_t)st * 2 * kPfTileBytes;
+        uint8_t* vt = kt + kPfTileBytes;
+        mbar_arrive_expect_tx(kv_full + st, 2 * kPfTileBytes);
+        tma_load_4d(kt, &tm_k, 0, j * kPfTile, kvh, b, kv_full + st);
+        tma_load_4d(kt + kPfTileBytes / 2, &tm_k, 64, j * kPfTile, kvh, b, kv_full + st);
+        tma_load_4d(vt, &tm_v, 0, j * kPfTile, kvh, b, kv_full + st);
+        tma_load_4d(vt + kPfTileBytes / 2, &tm_v, 64, j * kPfTile, kvh, b, kv_full + st);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 8) {
+    // ------------------------------------------------------------- MMA issue
+    if (lane == 0) {
+      constexpr uint32_t IS = idesc_pf<T>(false), IO = idesc_pf<T>(true);
+      auto issue_s = [&](int x, int j) {
+        const uint32_t qa = smem_u32(Qs + x * kPfTileBytes);
+        const uint32_t kb = smem_u32(KVs + (size_t)(j % kPf2Stages) * 2 * kPfTileBytes);
+        const uint32_t d = tmem + (uint32_t)x * 256;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ss(d, smem_desc_sw128(qa + (kk >> 2) * (kPfTileBytes / 2) + (kk & 3) * 32, 16, 1024),
+                     smem_desc_sw128(kb + (kk >> 2) * (kPfTileBytes / 2) + (kk & 3) * 32, 16, 1024), IS,
+                     kk > 0 ? 1u : 0u);
+        mma_commit(s_full + x);
+        PFTRACE(j, 4 + x);
+      };
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t vb = smem_u32(KVs + (size_t)(j % kPf2Stages) * 2 * kPfTileBytes + kPfTileBytes);
+        const uint32_t pa = tmem + (uint32_t)x * 256;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ts(tmem + (uint32_t)x * 256 + 128, pa + kk * 8, smem_desc_sw128(vb + kk * 2048, p.v_lbo, p.v_sbo),
+                     IO, (j > 0 || kk > 0) ? 1u : 0u);
+        PFTRACE(j, 6 + x);
+      };
+      int kv_seen = -1;                              // last key tile whose load was awaited
+      auto need_kv = [&](int j) -> bool {
+        if (kv_seen >= j) return true;
+        kv_seen = j;
+        if (!wait(kv_full + (j % kPf2Stages), (j / kPf2Stages) & 1, kDevWaitCopy)) return false;
+        tc_fence_after();
+        return true;
+      };
+      bool ok = wait(q_full, 0, kDevWaitCopy) && need_kv(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        if (has1) issue_s(1, 0);
+      }
+      for (int j = 0; ok && j < nk; ++j) {
+        for (int x = 0; x < 2 && ok; ++x) {
+          const int nx = x ? nk : n0;
+          if (x == 1 && !has1) break;
+          if (j >= nx) continue;
+          if (!wait(p_full + x, j & 1, kDevWaitMma)) { ok = false; break; }
+          tc_fence_after();
+          issue_pv(x, j);
+          if (j == nx - 1) {
+            mma_commit(o_done + x);
+          } else {
+            if (!need_kv(j + 1)) { ok = false; break; }
+            issue_s(x, j + 1);
+          }
+        }
+        if (ok) mma_commit(kv_empty + (j % kPf2Stages));
+      }
+      mma_commit(mma_done);
+      mbar_wait(mma_done, 0, lim);
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------------- softmax
+    const int x = warp >> 2;                       // query tile of this warpgroup
+    const int row = tid & 127;                     // TMEM lane == query row
+    const int qt = q0 + x;
+    const int nx = x ? nk : n0;
+    const int qpos = qt * kPfTile + row;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t sa = tmem + lane_base + (uint32_t)x * 256;    // S_j, then P_j
+    const uint32_t o_col = sa + 128;
+    float m_run = kNegBig, l_run = 0.f;
+    const float sl2 = p.scale_log2;
+    constexpr float kLazy = 2.f;                   // log2 of the largest weight (fp16 ex2 input precision)
+    bool ok = (x == 0 || has1);
+    for (int j = 0; ok && j < nx; ++j) {
+      if (!__all_sync(0xffffffffu, wait(s_full + x, j & 1, kDevWaitMma))) { ok = false; break; }
+      if (row == 0 && x == 0) PFTRACE(j, 8);
+      tc_fence_after();
+      float sv[128];
+      tmem_ld32x2(sa, sa + 32, sv, sv + 32);
+      tmem_ld32x2(sa + 64, sa + 96, sv + 64, sv + 96);
+      const bool diag = (j == qt);
+      const int kmax = diag ? row : 127;
+      float mq[4] = {kNegBig, kNegBig, kNegBig, kNegBig};
+      if (!diag) {
+#pragma unroll
+        for (int i = 0; i < 128; i += 4) {
+          mq[0] = fmaxf(mq[0], sv[i]);
+          mq[1] = fmaxf(mq[1], sv[i + 1]);
+          mq[2] = fmaxf(mq[2], sv[i + 2]);
+          mq[3] = fmaxf(mq[3], sv[i + 3]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) mq[i & 3] = (i <= kmax) ? fmaxf(mq[i & 3], sv[i]) : mq[i & 3];
+      }
+      const float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
+      if (j == 0) {
+        m_run = mt;
+      } else {
+        const bool need = mt > m_run + kLazy;
+        float alpha = 1.f;
+        if (need) {
+          alpha = fast_exp2(m_run - mt);
+          m_run = mt;
+          l_run *= alpha;
+        }
+        // O_X holds P_0 V_0 + ... + P_{j-1} V_{j-1}: the commit of S_X(j) covered them
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            float v[16];
+            tmem_ld16(o_col + c * 16, v);
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(v[i] * alpha);
+            tmem_st16(o_col + c * 16, w);
+          }
+        }
+      }
+      __half2 acc[4] = {__float2half2_rn(0.f), __float2half2_rn(0.f), __float2half2_rn(0.f),
+                        __float2half2_rn(0.f)};
+      auto weights = [&](auto masked) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int col = c * 32 + 2 * i;
+            float x0 = fmaf(sv[col], sl2, -m_run), x1 = fmaf(sv[col + 1], sl2, -m_run);
+            if constexpr (decltype(masked)::value) {
+              x0 = (col <= kmax) ? x0 : -INFINITY;
+              x1 = (col + 1 <= kmax) ? x1 : -INFINITY;
+            }
+            // half of the pairs on MUFU (packed fp16 ex2), half on the FMA pipe
+            uint32_t e;
+            if (i & 1) {
+              const float2 y = poly_exp2x2(make_float2(x0, x1));
+              e = f2_to_h2(y.x, y.y);
+            } else {
+              e = ex2_h2(f2_to_h2(x0, x1));
+            }
+            acc[i & 3] = __hadd2(acc[i & 3], *reinterpret_cast<const __half2*>(&e));
+            if constexpr (std::is_same<T, __half>::value) {
+              pk[i] = e;
+            } else {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&e));
+              pk[i] = pack2<__nv_bfloat16>(f.x, f.y);
+            }
+          }
+          tmem_st16(sa + c * 16, pk);                // P_j over the S_j row already read
+        }
+      };
+      if (diag)
+        weights(std::true_type());
+      else
+        weights(std::false_type());
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full + x);
+      if (row == 0 && x == 0) PFTRACE(j, 12);
+      const float2 s01 = __half22float2(__hadd2(acc[0], acc[1]));
+      const float2 s23 = __half22float2(__hadd2(acc[2], acc[3]));
+      l_run += (s01.x + s01.y) + (s23.x + s23.y);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, wait(o_done + x, 0, kDevWaitMma));
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.f / l_run;
+      const bool live = qpos < p.num_tokens;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(p.out);
+      const int64_t base = b * p.o_stride[0] + h * p.o_stride[1] + (int64_t)qpos * p.o_stride[2];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float v[16];
+        tmem_ld16(o_col + c * 16, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) v[i] *= inv;
+        if (!live) continue;
+        if (p.out_dtype == STARKV_F32) {
+          float4* d4 = reinterpret_cast<float4*>(dst + 4 * (base + c * 16));
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        } else {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 2 * (base + c * 16));
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            uint4 w;
+            if (p.out_dtype == STARKV_BF16) {
+              w.x = pack2<__nv_bfloat16>(v[8 * i], v[8 * i + 1]);
+              w.y = pack2<__nv_bfloat16>(v[8 * i + 2], v[8 * i + 3]);
+              w.z = pack2<__nv_bfloat16>(v[8 * i + 4], v[8 * i + 5]);
+              w.w = pack2<__nv_bfloat16>(v[8 * i + 6], v[8 * i + 7]);
+            } else {
+              w.x = pack2<__half>(v[8 * i], v[8 * i + 1]);
+              w.y = pack2<__half>(v[8 * i + 2], v[8 * i + 3]);
+              w.z = pack2<__half>(v[8 * i + 4], v[8 * i + 5]);
+              w.w = pack2<__half>(v[8 * i + 6], v[8 * i + 7]);
+            }
+            d4[i] = w;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace starkv

@@ -969,17 +969,17 @@ int starkv_prefill_attention(const starkv_prefill_args* a, starkv_stream_t strea
       (rc = prefill_map(&tk, a->k, a->dtype, a->batch, a->num_kv_heads, a->num_tokens, a->k_strides)) ||
       (rc = prefill_map(&tv, a->v, a->dtype, a->batch, a->num_kv_heads, a->num_tokens, a->v_strides)))
     return rc;
-  const int64_t ctas = (int64_t)p.n_qtiles * a->num_q_heads * a->batch;
+  const int64_t ctas = (int64_t)((p.n_qtiles + 1) / 2) * a->num_q_heads * a->batch;
   if (ctas > 0x7fffffff) return set_error(STARKV_ERR_UNSUPPORTED, "too many query tiles");
   cudaStream_t st = (cudaStream_t)stream;
   if (a->dtype == STARKV_F16) {
-    rc = ensure_smem(prefill_attn_kernel<__half>, kPfSmem, 24);
+    rc = ensure_smem(prefill_attn2_kernel<__half>, kPf2Smem, 24);
     if (rc) return rc;
-    prefill_attn_kernel<__half><<<(unsigned)ctas, kPfThreads, kPfSmem, st>>>(p, tq, tk, tv);
+    prefill_attn2_kernel<__half><<<(unsigned)ctas, kPf2Threads, kPf2Smem, st>>>(p, tq, tk, tv);
   } else {
-    rc = ensure_smem(prefill_attn_kernel<__nv_bfloat16>, kPfSmem, 25);
+    rc = ensure_smem(prefill_attn2_kernel<__nv_bfloat16>, kPf2Smem, 25);
     if (rc) return rc;
-    prefill_attn_kernel<__nv_bfloat16><<<(unsigned)ctas, kPfThreads, kPfSmem, st>>>(p, tq, tk, tv);
+    prefill_attn2_kernel<__nv_bfloat16><<<(unsigned)ctas, kPf2Threads, kPf2Smem, st>>>(p, tq, tk, tv);
   }
   return fail_launch();
 }
