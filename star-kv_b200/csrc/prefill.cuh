@@ -488,12 +488,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 // alternates between them.  TMEM: tile X in {0, 1} owns columns 256X..256X+255
 // — S_j (fp32, 128 columns) at +0, overwritten by P_j (16-bit pairs, 64
 // columns) once its row has been read, and the output accumulator at +128.
-// One thread issues every MMA, so they execute in issue order: S_X(j+1) is
-// issued after P_X(j) V_j and may overwrite the P_X(j) it reads, and the commit
-// that announces S_X(j+1) also covers P_X(j) V_j (the softmax may then rescale
-// O_X and write P_X(j+1)).  Warps 0-3 own tile 0, warps 4-7 tile 1, one thread
-// per query row holding the whole S row: no cross-thread exchange.
-constexpr int kPf2Threads = 320;
+// Warp 8 issues S = Q K^T, warp 10 issues O += P V (two issuing threads: one
+// thread issues an M = N = 128 MMA only every ~120 cycles); S_X(j+1) overwrites
+// P_X(j), so its issuer first waits for P_X(j) V_j to complete, which also
+// makes O_X safe for the softmax to rescale once it sees S_X(j+1).  Warp 9
+// loads tiles by TMA.  Warps 0-3 own tile 0, warps 4-7 tile 1, one thread per
+// query row holding the whole S row: no cross-thread exchange.
+constexpr int kPf2Threads = 352;
 constexpr int kPf2Stages = 2;
 constexpr size_t kPf2Smem = kPfHeader + (2 + 2 * kPf2Stages) * (size_t)kPfTileBytes;
 
@@ -508,8 +509,9 @@ __global__ void __launch_bounds__(kPf2Threads, 1)
   uint64_t* kv_empty = bar + 3;    // [2]
   uint64_t* s_full = bar + 5;      // [2]: per query tile
   uint64_t* p_full = bar + 7;      // [2]: per query tile
-  uint64_t* o_done = bar + 9;      // [2]: per query tile, last P V complete
-  uint64_t* mma_done = bar + 11;
+  uint64_t* pv_done = bar + 9;     // [2]: per query tile, its latest P V complete
+  uint64_t* s_done = bar + 11;     // S issuer's MMAs complete (teardown)
+  uint64_t* o_done = bar + 12;     // P V issuer's MMAs complete (teardown)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 256);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 260);
   uint8_t* Qs = smem + kPfHeader;                  // tile X at X * kPfTileBytes
@@ -535,9 +537,10 @@ __global__ void __launch_bounds__(kPf2Threads, 1)
       mbar_init(kv_empty + s, 1);
       mbar_init(s_full + s, 1);
       mbar_init(p_full + s, 128);
-      mbar_init(o_done + s, 1);
+      mbar_init(pv_done + s, 1);
     }
-    mbar_init(mma_done, 1);
+    mbar_init(s_done, 1);
+    mbar_init(o_done, 1);
     *s_abort = 0;
     fence_mbar_init();
   }
@@ -580,63 +583,57 @@ __global__ void __launch_bounds__(kPf2Threads, 1)
     }
     __syncwarp();
   } else if (warp == 8) {
-    // ------------------------------------------------------------- MMA issue
+    // ------------------------------------------------------------ S = Q K^T
     if (lane == 0) {
-      constexpr uint32_t IS = idesc_pf<T>(false), IO = idesc_pf<T>(true);
-      auto issue_s = [&](int x, int j) {
-        const uint32_t qa = smem_u32(Qs + x * kPfTileBytes);
-        const uint32_t kb = smem_u32(KVs + (size_t)(j % kPf2Stages) * 2 * kPfTileBytes);
-        const uint32_t d = tmem + (uint32_t)x * 256;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ss(d, smem_desc_sw128(qa + (kk >> 2) * (kPfTileBytes / 2) + (kk & 3) * 32, 16, 1024),
-                     smem_desc_sw128(kb + (kk >> 2) * (kPfTileBytes / 2) + (kk & 3) * 32, 16, 1024), IS,
-                     kk > 0 ? 1u : 0u);
-        mma_commit(s_full + x);
-        PFTRACE(j, 4 + x);
-      };
-      auto issue_pv = [&](int x, int j) {
-        const uint32_t vb = smem_u32(KVs + (size_t)(j % kPf2Stages) * 2 * kPfTileBytes + kPfTileBytes);
-        const uint32_t pa = tmem + (uint32_t)x * 256;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ts(tmem + (uint32_t)x * 256 + 128, pa + kk * 8, smem_desc_sw128(vb + kk * 2048, p.v_lbo, p.v_sbo),
-                     IO, (j > 0 || kk > 0) ? 1u : 0u);
-        PFTRACE(j, 6 + x);
-      };
-      int kv_seen = -1;                              // last key tile whose load was awaited
-      auto need_kv = [&](int j) -> bool {
-        if (kv_seen >= j) return true;
-        kv_seen = j;
-        if (!wait(kv_full + (j % kPf2Stages), (j / kPf2Stages) & 1, kDevWaitCopy)) return false;
-        tc_fence_after();
-        return true;
-      };
-      bool ok = wait(q_full, 0, kDevWaitCopy) && need_kv(0);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0, 0);
-        if (has1) issue_s(1, 0);
-      }
+      constexpr uint32_t IS = idesc_pf<T>(false);
+      bool ok = wait(q_full, 0, kDevWaitCopy);
       for (int j = 0; ok && j < nk; ++j) {
-        for (int x = 0; x < 2 && ok; ++x) {
-          const int nx = x ? nk : n0;
-          if (x == 1 && !has1) break;
-          if (j >= nx) continue;
+        if (!wait(kv_full + (j % kPf2Stages), (j / kPf2Stages) & 1, kDevWaitCopy)) break;
+        const uint32_t kb = smem_u32(KVs + (size_t)(j % kPf2Stages) * 2 * kPfTileBytes);
+        for (int x = 0; x < (has1 ? 2 : 1); ++x) {
+          if (j >= (x ? nk : n0)) continue;
+          // S_x(j) overwrites P_x(j-1): wait for P_x(j-1) V_{j-1} to complete
+          if (j >= 1 && !wait(pv_done + x, (j - 1) & 1, kDevWaitMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t qa = smem_u32(Qs + x * kPfTileBytes);
+          const uint32_t d = tmem + (uint32_t)x * 256;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_f16_ss(d, smem_desc_sw128(qa + (kk >> 2) * (kPfTileBytes / 2) + (kk & 3) * 32, 16, 1024),
+                       smem_desc_sw128(kb + (kk >> 2) * (kPfTileBytes / 2) + (kk & 3) * 32, 16, 1024), IS,
+                       kk > 0 ? 1u : 0u);
+          mma_commit(s_full + x);
+          PFTRACE(j, 4 + x);
+        }
+      }
+      mma_commit(s_done);
+      mbar_wait(s_done, 0, lim);
+    }
+    __syncwarp();
+  } else if (warp == 10) {
+    // ------------------------------------------------------------ O += P V
+    if (lane == 0) {
+      constexpr uint32_t IO = idesc_pf<T>(true);
+      bool ok = true;
+      for (int j = 0; ok && j < nk; ++j) {
+        const uint32_t vb = smem_u32(KVs + (size_t)(j % kPf2Stages) * 2 * kPfTileBytes + kPfTileBytes);
+        for (int x = 0; x < (has1 ? 2 : 1); ++x) {
+          if (j >= (x ? nk : n0)) continue;
           if (!wait(p_full + x, j & 1, kDevWaitMma)) { ok = false; break; }
           tc_fence_after();
-          issue_pv(x, j);
-          if (j == nx - 1) {
-            mma_commit(o_done + x);
-          } else {
-            if (!need_kv(j + 1)) { ok = false; break; }
-            issue_s(x, j + 1);
-          }
+          const uint32_t pa = tmem + (uint32_t)x * 256;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            mma_f16_ts(pa + 128, pa + kk * 8, smem_desc_sw128(vb + kk * 2048, p.v_lbo, p.v_sbo), IO,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(pv_done + x);
+          PFTRACE(j, 6 + x);
         }
+        // S_x(j) finished before the softmax released P_x(j): the stage is free after these P V
         if (ok) mma_commit(kv_empty + (j % kPf2Stages));
       }
-      mma_commit(mma_done);
-      mbar_wait(mma_done, 0, lim);
+      mma_commit(o_done);
+      mbar_wait(o_done, 0, lim);
     }
     __syncwarp();
   } else {
@@ -686,7 +683,7 @@ __global__ void __launch_bounds__(kPf2Threads, 1)
           m_run = mt;
           l_run *= alpha;
         }
-        // O_X holds P_0 V_0 + ... + P_{j-1} V_{j-1}: the commit of S_X(j) covered them
+        // O_X holds P_0 V_0 + ... + P_{j-1} V_{j-1}: S_X(j) was issued after they completed
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -744,7 +741,7 @@ __global__ void __launch_bounds__(kPf2Threads, 1)
       const float2 s23 = __half22float2(__hadd2(acc[2], acc[3]));
       l_run += (s01.x + s01.y) + (s23.x + s23.y);
     }
-    if (ok) ok = __all_sync(0xffffffffu, wait(o_done + x, 0, kDevWaitMma));
+    if (ok) ok = __all_sync(0xffffffffu, wait(pv_done + x, (nx - 1) & 1, kDevWaitMma));
     if (ok) {
       tc_fence_after();
       const float inv = 1.f / l_run;
