@@ -3,36 +3,26 @@
 // The reference's prompt path rebuilds full K / V from the latents
 // (K = RoPE(X_k U_k^T), V = X_v U_v^T) and runs causal SDPA over them
 // (model.py:429-449, LlamaLoRaAttention_headwise.py:100-116).  This kernel is the
-// attention half of that: causal flash attention with the online softmax, one
-// CTA per (128-query tile, query head, sequence), K / V of the query head's KV
-// head (GQA by index), q / k / v / out as strided (B, H, T, 128) views so that
-// the projections' (B, T, H, 128) tensors are read and written in place.
+// attention half of that: causal flash attention with the online softmax, K / V
+// of the query head's KV head (GQA by index), q / k / v / out as strided
+// (B, H, T, 128) views so that the projections' (B, T, H, 128) tensors are read
+// and written in place.
 //
-// Roles (352 threads, one CTA per SM: it holds all 512 TMEM columns and 227 KB
-// of shared memory):
-//   * warps 0-7: softmax.  Query row r is shared by thread r (key columns 0-63
-//     of every tile) and thread 128 + r (columns 64-127), both on TMEM lane r.
-//     S_j = Q K_j^T lands in TMEM (fp32, 128 columns, two buffers); both
-//     threads of a row read the whole row, so each forms the row maximum itself,
-//     and each writes the weights of its own 64 keys: x = S * scale - m in
-//     fp32, 2^x by a packed MUFU ex2 of the fp16-rounded pair for half of the
-//     pairs and by a packed fp32x2 polynomial on the FMA pipe for the other
-//     half (MUFU alone paces the tile otherwise); the fp16 results are P_j
-//     itself, or are rounded to bf16, and go back to TMEM as the
-//     16-bit A operand (64 columns, two buffers).  The output O accumulates in
-//     TMEM across tiles (P_j V_j with accumulate).  The running maximum m of a
-//     row moves only when a tile's maximum exceeds it by more than 2^2 (so x <= 2,
-//     where fp16 holds x to 2^-10): then the row's O and l are scaled by
-//     exp2(m_old - m_new) in place, after P_{j-1} V_{j-1} has completed.  The
-//     two halves' sums l meet once, at the end, through shared memory.
-//   * warp 8 lane 0 issues S_j = Q K_j^T (8 tcgen05.mma, M = N = 128, K = 16);
-//     warp 9 lane 0 issues O += P_j V_j (A = P_j from TMEM, V_j MN-major).  Two
-//     issuing threads keep the tensor core at its rate for N = 128.
-//   * warp 10 lane 0: TMA loads of the Q tile and of a three-stage ring of
-//     (K_j, V_j) tiles, each tile two 64-channel x 128-row boxes in the 128-byte
-//     swizzled layout, which is the canonical K-major layout for Q and K and the
-//     MN-major one for V (channels along N, tokens along K: no transposition).
-//     Rows past the sequence end are filled with zeros by the TMA unit.
+// CTA = (pair of 128-query tiles 2i and 2i+1, query head, sequence), heaviest
+// pairs first, 352 threads, one CTA per SM (all 512 TMEM columns):
+//   * warp 9 lane 0: TMA loads of the two Q tiles and of a two-stage ring of
+//     (K_j, V_j) tiles shared by both query tiles, each tile two 64-channel x
+//     128-row boxes in the 128-byte swizzled layout — the canonical K-major
+//     layout for Q and K and the MN-major one for V (channels along N, tokens
+//     along K: no transposition).  Rows past the sequence end are zero-filled.
+//   * warp 8 lane 0 issues S_X(j) = Q_X K_j^T, warp 10 lane 0 issues
+//     O_X += P_X(j) V_j (8 tcgen05.mma each, M = N = 128, K = 16; A = P from TMEM).
+//   * warps 0-3 (query tile 0) and 4-7 (tile 1), one thread per query row
+//     holding the whole S row: row maximum (lazy: the running maximum moves only
+//     when a tile exceeds it by more than 2^2, then O and l of that row are
+//     rescaled in TMEM), weights x = S * scale - m in fp32 and 2^x by a packed
+//     fp16 MUFU ex2 for half of the pairs and a packed fp32x2 polynomial on the
+//     FMA pipe for the other half, written as 16-bit P over the S row in TMEM.
 // Every wait is bounded (mbarriers only, no named barriers); a wait that runs
 // out records an error code, sets the CTA's abort flag and the roles leave
 // their loops.
@@ -48,15 +38,9 @@
 
 namespace starkv {
 
-constexpr int kPfThreads = 352;
-constexpr int kPfTile = 128;                    // queries per CTA and keys per step
+constexpr int kPfTile = 128;                    // queries per query tile and keys per step
 constexpr int kPfTileBytes = 128 * 128 * 2;     // one 128 x 128 16-bit tile
-constexpr int kPfHeader = 3072;                 // barriers, TMEM address, abort flag, row exchange
-constexpr int kPfStages = 3;                    // (K, V) tile ring
-constexpr size_t kPfSmem = kPfHeader + (1 + 2 * kPfStages) * (size_t)kPfTileBytes;   // Q + ring
-
-// TMEM columns: S buffers, the output accumulator and the P buffers (16-bit pairs).
-constexpr uint32_t kPfColS = 0, kPfColO = 256, kPfColP = 384;
+constexpr int kPfHeader = 3072;                 // barriers, TMEM address, abort flag
 
 struct PrefillParams {
   const void* q;
@@ -127,6 +111,13 @@ __device__ __forceinline__ float2 poly_exp2x2(float2 x) {
   return make_float2(__uint_as_float(__float_as_uint(q.x) + ex), __uint_as_float(__float_as_uint(q.y) + ey));
 }
 
+// max(a, b, c) in one instruction (three-input max.f32, sm_100).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t f2_to_h2(float a, float b) {
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -160,326 +151,6 @@ template <>
 __device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kPfThreads, 1)
-    prefill_attn_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap tm_q,
-                        const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-  uint64_t* q_full = bar + 0;
-  uint64_t* kv_full = bar + 1;     // [3]
-  uint64_t* kv_empty = bar + 4;    // [3]
-  uint64_t* s_full = bar + 7;      // [2]
-  uint64_t* p_full = bar + 9;      // [2]
-  uint64_t* o_done = bar + 11;     // [2]: P_j V_j complete, j mod 2
-  uint64_t* s_done = bar + 13;     // S issuer's MMAs complete (teardown)
-  uint64_t* pv_done = bar + 14;    // P V issuer's MMAs complete (teardown)
-  uint64_t* xchg = bar + 15;       // [2]: both halves of every row wrote their partial, j mod 2
-  float* red = reinterpret_cast<float*>(smem + 1024);   // [2][2][128] row partials
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + 256);
-  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + 260);
-  uint8_t* Qs = smem + kPfHeader;
-  uint8_t* KVs = Qs + kPfTileBytes;    // stage s: K tile at 2*s, V tile at 2*s+1
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int per = p.num_q_heads * p.batch;
-  const int cta = blockIdx.x;
-  const int qt = p.n_qtiles - 1 - cta / per;      // heaviest query tiles first
-  const int h = (cta % per) % p.num_q_heads;
-  const int b = (cta % per) / p.num_q_heads;
-  const int kvh = h / (p.num_q_heads / p.num_kv_heads);
-  const int n = qt + 1;                            // causal: key tiles 0..qt
-  const unsigned long long lim = p.wait_ns;
-
-  if (tid == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < kPfStages; ++s) {
-      mbar_init(kv_full + s, 1);
-      mbar_init(kv_empty + s, 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(s_full + s, 1);
-      mbar_init(p_full + s, 256);
-      mbar_init(o_done + s, 1);
-      mbar_init(xchg + s, 256);
-    }
-    mbar_init(s_done, 1);
-    mbar_init(pv_done, 1);
-    *s_abort = 0;
-    fence_mbar_init();
-  }
-  if (warp == 8) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  auto wait = [&](uint64_t* bar_, uint32_t parity, int code) -> bool {
-    if (*s_abort) return false;
-    if (mbar_wait(bar_, parity, lim)) return true;
-    record_error(p.err, code);
-    *s_abort = 1;
-    return false;
-  };
-
-  if (warp == 10) {
-    // ---------------------------------------------------------------- producer
-    if (lane == 0) {
-      // a tile is two 64-channel boxes of 128 rows (128-byte swizzle), 16 KB each
-      mbar_arrive_expect_tx(q_full, kPfTileBytes);
-      tma_load_4d(Qs, &tm_q, 0, qt * kPfTile, h, b, q_full);
-      tma_load_4d(Qs + kPfTileBytes / 2, &tm_q, 64, qt * kPfTile, h, b, q_full);
-      for (int j = 0; j < n; ++j) {
-        const int st = j % kPfStages;
-        if (j >= kPfStages && !wait(kv_empty + st, ((j / kPfStages) - 1) & 1, kDevWaitMma)) break;
-        if (j >= kPfStages) PFTRACE(j, 1);
-        uint8_t* kt = KVs + (size_t)st * 2 * kPfTileBytes;
-        uint8_t* vt = kt + kPfTileBytes;
-        mbar_arrive_expect_tx(kv_full + st, 2 * kPfTileBytes);
-        tma_load_4d(kt, &tm_k, 0, j * kPfTile, kvh, b, kv_full + st);
-        tma_load_4d(kt + kPfTileBytes / 2, &tm_k, 64, j * kPfTile, kvh, b, kv_full + st);
-        tma_load_4d(vt, &tm_v, 0, j * kPfTile, kvh, b, kv_full + st);
-        tma_load_4d(vt + kPfTileBytes / 2, &tm_v, 64, j * kPfTile, kvh, b, kv_full + st);
-        PFTRACE(j, 2);
-      }
-    }
-    __syncwarp();
-  } else if (warp == 8) {
-    // ------------------------------------------------------------ S = Q K^T
-    if (lane == 0) {
-      constexpr uint32_t IS = idesc_pf<T>(false);
-      const uint32_t qa = smem_u32(Qs);
-      bool ok = wait(q_full, 0, kDevWaitCopy);
-      for (int j = 0; ok && j < n; ++j) {
-        if (!wait(kv_full + (j % kPfStages), (j / kPfStages) & 1, kDevWaitCopy)) break;
-        // S buffer j mod 2 was read by the softmax for tile j-2
-        PFTRACE(j, 3);                             // tile j present
-        if (j >= 2 && !wait(p_full + (j & 1), ((j - 2) >> 1) & 1, kDevWaitMma)) break;
-        PFTRACE(j, 4);                             // S buffer free
-        tc_fence_after();
-        const uint32_t kb = smem_u32(KVs + (size_t)(j % kPfStages) * 2 * kPfTileBytes);
-        const uint32_t d = tmem + kPfColS + (uint32_t)(j & 1) * 128;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ss(d, smem_desc_sw128(qa + (kk >> 2) * (kPfTileBytes / 2) + (kk & 3) * 32, 16, 1024),
-                     smem_desc_sw128(kb + (kk >> 2) * (kPfTileBytes / 2) + (kk & 3) * 32, 16, 1024), IS,
-                     kk > 0 ? 1u : 0u);
-        mma_commit(s_full + (j & 1));
-        PFTRACE(j, 5);                             // S_j issued
-      }
-      mma_commit(s_done);
-      mbar_wait(s_done, 0, lim);
-    }
-    __syncwarp();
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ O += P V
-    if (lane == 0) {
-      constexpr uint32_t IO = idesc_pf<T>(true);
-      for (int j = 0; j < n; ++j) {
-        if (!wait(p_full + (j & 1), (j >> 1) & 1, kDevWaitMma)) break;
-        PFTRACE(j, 6);                             // P_j ready
-        tc_fence_after();
-        const uint32_t vb = smem_u32(KVs + (size_t)(j % kPfStages) * 2 * kPfTileBytes + kPfTileBytes);
-        const uint32_t pa = tmem + kPfColP + (uint32_t)(j & 1) * 64;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ts(tmem + kPfColO, pa + kk * 8, smem_desc_sw128(vb + kk * 2048, p.v_lbo, p.v_sbo), IO,
-                     (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(o_done + (j & 1));
-        mma_commit(kv_empty + (j % kPfStages));
-        PFTRACE(j, 7);                             // P_j V_j issued
-      }
-      mma_commit(pv_done);
-      mbar_wait(pv_done, 0, lim);
-    }
-    __syncwarp();
-  } else {
-    // ---------------------------------------------------------------- softmax
-    const int row = tid & 127, half = tid >> 7;     // TMEM lane == query row
-    const int qpos = qt * kPfTile + row;
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t o_col = tmem + lane_base + kPfColO + half * 64;
-    float m_run = kNegBig, l_run = 0.f;
-    const float sl2 = p.scale_log2;
-    constexpr float kLazy = 2.f;                     // log2 of the largest weight (fp16 ex2 input precision)
-    // trade a per-row partial with the other half of the row (slot k mod 2, phase k / 2)
-    auto trade = [&](int k, float v) -> float {
-      float* r = red + (k & 1) * 256;
-      r[half * 128 + row] = v;
-      mbar_arrive(xchg + (k & 1));
-      if (!wait(xchg + (k & 1), (k >> 1) & 1, kDevWaitMma)) return NAN;
-      return r[(half ^ 1) * 128 + row];
-    };
-    bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      if (!__all_sync(0xffffffffu, wait(s_full + (j & 1), (j >> 1) & 1, kDevWaitMma))) { ok = false; break; }
-      if (tid == 0) PFTRACE(j, 8);                 // S_j complete
-      tc_fence_after();
-      // both threads of a row read the whole row: the row maximum needs no exchange
-      const uint32_t sa = tmem + lane_base + kPfColS + (uint32_t)(j & 1) * 128;
-      float sv[64], so[64];                            // own half, other half
-      tmem_ld32x2(sa + half * 64, sa + half * 64 + 32, sv, sv + 32);
-      tmem_ld32x2(sa + (half ^ 1) * 64, sa + (half ^ 1) * 64 + 32, so, so + 32);
-      const bool diag = (j == qt);
-      const int kmax = diag ? row - half * 64 : 63;            // last kept column of the own half
-      const int kmax_o = diag ? row - (half ^ 1) * 64 : 63;    // ... of the other half
-      float mq[4] = {kNegBig, kNegBig, kNegBig, kNegBig};
-      if (!diag) {                                     // no masking off the diagonal
-#pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          mq[0] = fmaxf(mq[0], sv[i]);
-          mq[1] = fmaxf(mq[1], sv[i + 1]);
-          mq[2] = fmaxf(mq[2], so[i]);
-          mq[3] = fmaxf(mq[3], so[i + 1]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          mq[i & 1] = (i <= kmax) ? fmaxf(mq[i & 1], sv[i]) : mq[i & 1];
-          mq[2 + (i & 1)] = (i <= kmax_o) ? fmaxf(mq[2 + (i & 1)], so[i]) : mq[2 + (i & 1)];
-        }
-      }
-      if (tid == 0) PFTRACE(j, 9);                 // S_j loaded, row max
-      const float mt = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
-      if (j == 0) {
-        m_run = mt;
-      } else {
-        const bool need = mt > m_run + kLazy;
-        float alpha = 1.f;
-        if (need) {
-          alpha = fast_exp2(m_run - mt);
-          m_run = mt;
-          l_run *= alpha;
-        }
-        if (__any_sync(0xffffffffu, need)) {
-          // O holds P_0 V_0 + ... + P_{j-1} V_{j-1} once P_{j-1} V_{j-1} completes
-          if (!__all_sync(0xffffffffu, wait(o_done + ((j - 1) & 1), ((j - 1) >> 1) & 1, kDevWaitMma))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float v[16];
-            tmem_ld16(o_col + c * 16, v);
-            uint32_t w[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(v[i] * alpha);
-            tmem_st16(o_col + c * 16, w);
-          }
-        }
-      }
-      // P buffer j mod 2 was read by P_{j-2} V_{j-2}
-      if (j >= 2 && !__all_sync(0xffffffffu, wait(o_done + (j & 1), ((j - 2) >> 1) & 1, kDevWaitMma))) {
-        ok = false;
-        break;
-      }
-      if (tid == 0) PFTRACE(j, 11);                // rescale done, P buffer free
-      // weights: x = s * scale - m in fp32 (x <= kLazy), rounded to fp16 pairs,
-      // one packed MUFU ex2 per pair; masked keys get x = -inf (weight 0)
-      __half2 acc[4] = {__float2half2_rn(0.f), __float2half2_rn(0.f), __float2half2_rn(0.f),
-                        __float2half2_rn(0.f)};
-      const uint32_t pcol = tmem + lane_base + kPfColP + (uint32_t)(j & 1) * 64 + half * 32;
-      auto weights = [&](auto masked) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int col = c * 32 + 2 * i;
-            float x0 = fmaf(sv[col], sl2, -m_run), x1 = fmaf(sv[col + 1], sl2, -m_run);
-            if constexpr (decltype(masked)::value) {
-              x0 = (col <= kmax) ? x0 : -INFINITY;
-              x1 = (col + 1 <= kmax) ? x1 : -INFINITY;
-            }
-            // half of the pairs on MUFU (packed fp16 ex2), half on the FMA pipe
-            uint32_t e;
-            if (i & 1) {
-              const float2 y = poly_exp2x2(make_float2(x0, x1));
-              e = f2_to_h2(y.x, y.y);
-            } else {
-              e = ex2_h2(f2_to_h2(x0, x1));
-            }
-            acc[i & 3] = __hadd2(acc[i & 3], *reinterpret_cast<const __half2*>(&e));
-            if constexpr (std::is_same<T, __half>::value) {
-              pk[i] = e;
-            } else {
-              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&e));
-              pk[i] = pack2<__nv_bfloat16>(f.x, f.y);
-            }
-          }
-          tmem_st16(pcol + c * 16, pk);
-        }
-      };
-      if (diag)
-        weights(std::true_type());
-      else
-        weights(std::false_type());
-      const float2 s01 = __half22float2(__hadd2(acc[0], acc[1]));
-      const float2 s23 = __half22float2(__hadd2(acc[2], acc[3]));
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(p_full + (j & 1));
-      if (tid == 0) PFTRACE(j, 12);                // P_j written
-      l_run += (s01.x + s01.y) + (s23.x + s23.y);
-    }
-    if (ok) ok = __all_sync(0xffffffffu, wait(o_done + ((n - 1) & 1), ((n - 1) >> 1) & 1, kDevWaitMma));
-    float l_tot = 0.f;
-    if (ok) {
-      const float other = trade(0, l_run);
-      ok = __all_sync(0xffffffffu, !isnan(other));
-      l_tot = l_run + other;
-    }
-    if (ok) {
-      tc_fence_after();
-      const float inv = 1.f / l_tot;
-      const bool live = qpos < p.num_tokens;
-      uint8_t* dst = reinterpret_cast<uint8_t*>(p.out);
-      const int64_t base = b * p.o_stride[0] + h * p.o_stride[1] + (int64_t)qpos * p.o_stride[2] + half * 64;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[16];
-        tmem_ld16(o_col + c * 16, v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) v[i] *= inv;
-        if (!live) continue;
-        if (p.out_dtype == STARKV_F32) {
-          float4* d4 = reinterpret_cast<float4*>(dst + 4 * (base + c * 16));
-#pragma unroll
-          for (int i = 0; i < 4; ++i) d4[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-        } else {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 2 * (base + c * 16));
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            uint4 w;
-            if (p.out_dtype == STARKV_BF16) {
-              w.x = pack2<__nv_bfloat16>(v[8 * i], v[8 * i + 1]);
-              w.y = pack2<__nv_bfloat16>(v[8 * i + 2], v[8 * i + 3]);
-              w.z = pack2<__nv_bfloat16>(v[8 * i + 4], v[8 * i + 5]);
-              w.w = pack2<__nv_bfloat16>(v[8 * i + 6], v[8 * i + 7]);
-            } else {
-              w.x = pack2<__half>(v[8 * i], v[8 * i + 1]);
-              w.y = pack2<__half>(v[8 * i + 2], v[8 * i + 3]);
-              w.z = pack2<__half>(v[8 * i + 4], v[8 * i + 5]);
-              w.w = pack2<__half>(v[8 * i + 6], v[8 * i + 7]);
-            }
-            d4[i] = w;
-          }
-        }
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 8) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
 }
 
 // ---------------------------------------------------------------------------
@@ -662,11 +333,11 @@ __global__ void __launch_bounds__(kPf2Threads, 1)
       float mq[4] = {kNegBig, kNegBig, kNegBig, kNegBig};
       if (!diag) {
 #pragma unroll
-        for (int i = 0; i < 128; i += 4) {
-          mq[0] = fmaxf(mq[0], sv[i]);
-          mq[1] = fmaxf(mq[1], sv[i + 1]);
-          mq[2] = fmaxf(mq[2], sv[i + 2]);
-          mq[3] = fmaxf(mq[3], sv[i + 3]);
+        for (int i = 0; i < 128; i += 8) {
+          mq[0] = max3(mq[0], sv[i], sv[i + 1]);
+          mq[1] = max3(mq[1], sv[i + 2], sv[i + 3]);
+          mq[2] = max3(mq[2], sv[i + 4], sv[i + 5]);
+          mq[3] = max3(mq[3], sv[i + 6], sv[i + 7]);
         }
       } else {
 #pragma unroll
