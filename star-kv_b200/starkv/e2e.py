@@ -29,7 +29,7 @@ from typing import List, Optional, Sequence
 import numpy as np
 import torch
 
-from .attention import LlamaCustomAttention, LlamaCustomAttentionQuant, StarKVCache
+from .attention import LlamaCustomAttention, LlamaCustomAttentionQuant, StarKVCache, apply_rotary_pos_emb_custom
 from .export import BlockVProj, RaggedKProj
 
 
@@ -117,6 +117,108 @@ def generate(model, prompt: torch.Tensor, new_tokens: int, capacity: int = 0, st
     return torch.cat(out, dim=1), per_tok
 
 
+@torch.no_grad()
+def generate_graphed(model, prompt: torch.Tensor, new_tokens: int, capacity: int = 0,
+                     stats: Optional[dict] = None):
+    """``generate`` with each decode step's dense work replayed from CUDA graphs.
+
+    The attention call of a step takes its token count from the host (the kernels'
+    grids and split partitions depend on it), so it stays outside the graphs; the
+    rest of a layer is captured once: graph A_i (input norm, q_proj, RoPE of the
+    query) and graph B_i (o_proj, residual, post-attention norm, MLP, residual),
+    plus one graph for the token embedding and RoPE tables and one for the LM
+    head and argmax.  A step is then 2 + 2L graph launches and 2L C-ABI calls
+    (``starkv_project_append`` + ``starkv_decode_attention`` per layer) on the
+    current stream, all on static buffers.  Returns what ``generate`` returns,
+    with the same tokens."""
+    B, P = prompt.shape
+    quant = getattr(model, "starkv_quantized", True)
+    cache = StarKVCache(capacity or P + new_tokens, quantized=quant)
+    dev = prompt.device
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    logits = forward_tokens(model, prompt, 0, cache)
+    p1.record()
+    tok = logits.argmax(-1, keepdim=True)
+    out: List[torch.Tensor] = [tok]
+    layers = model.model.layers
+    dt = model.model.embed_tokens.weight.dtype
+    attn0 = layers[0].self_attn
+    Hq, D = attn0.num_heads, attn0.head_dim
+    tok_s = tok.clone()
+    pos_s = torch.full((B, 1), P, dtype=torch.long, device=dev)
+    h_s = torch.empty(B, 1, model.config.hidden_size, dtype=dt, device=dev)
+    x_s = torch.empty_like(h_s)
+    q_s = torch.empty(B, Hq, D, dtype=dt, device=dev)
+    attn_s = torch.empty(B, Hq, D, dtype=dt, device=dev)
+    cos_s = torch.empty(B, 1, D, dtype=dt, device=dev)
+    sin_s = torch.empty_like(cos_s)
+    vs = [(l.self_attn.k_proj.VS.weight.to(dt).contiguous(), l.self_attn.v_proj.VS.weight.to(dt).contiguous())
+          for l in layers]
+    states = [cache.layer(i, l.self_attn, B, dt) for i, l in enumerate(layers)]
+
+    def embed():
+        h_s.copy_(model.model.embed_tokens(tok_s))
+        c, s_ = model.model.rotary_emb(h_s, pos_s)
+        cos_s.copy_(c)
+        sin_s.copy_(s_)
+
+    def pre(i):
+        layer = layers[i]
+        x_s.copy_(layer.input_layernorm(h_s))
+        q = layer.self_attn.q_proj(x_s).view(B, 1, Hq, D).transpose(1, 2)
+        q_s.copy_(apply_rotary_pos_emb_custom(q, cos_s, sin_s)[:, :, 0, :])
+
+    def post(i):
+        layer = layers[i]
+        h_s.add_(layer.self_attn.o_proj(attn_s.reshape(B, 1, Hq * D)))
+        h_s.add_(layer.mlp(layer.post_attention_layernorm(h_s)))
+
+    def head():
+        lg = model.lm_head(model.model.norm(h_s))[:, 0]
+        tok_s.copy_(lg.argmax(-1, keepdim=True))
+        pos_s.add_(1)
+
+    fns = [embed] + [(lambda i=i: pre(i)) for i in range(len(layers))] + \
+          [(lambda i=i: post(i)) for i in range(len(layers))] + [head]
+    # warm the captured ops on a side stream (allocator pools, cuBLAS handles), as torch requires
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    saved = (tok_s.clone(), pos_s.clone())
+    with torch.cuda.stream(side):
+        for f in fns:
+            f()
+    torch.cuda.current_stream().wait_stream(side)
+    tok_s.copy_(saved[0])
+    pos_s.copy_(saved[1])
+    graphs = []
+    pool = None
+    for f in fns:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=pool):
+            f()
+        pool = g.pool()
+        graphs.append(g)
+    g_embed, g_pre, g_post, g_head = graphs[0], graphs[1:1 + len(layers)], graphs[1 + len(layers):-1], graphs[-1]
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(new_tokens - 1):
+        g_embed.replay()
+        for i, st in enumerate(states):
+            g_pre[i].replay()
+            st.step_from_hidden(q_s, x_s, vs[i][0], vs[i][1], out=attn_s)
+            g_post[i].replay()
+        g_head.replay()
+        out.append(tok_s.clone())
+    e1.record()
+    torch.cuda.synchronize()
+    per_tok = e0.elapsed_time(e1) / 1e3 / max(1, new_tokens - 1)
+    if stats is not None:
+        stats["prompt_s"] = p0.elapsed_time(p1) / 1e3
+    return torch.cat(out, dim=1), per_tok
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--layers", type=int, default=32)
@@ -125,17 +227,19 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--unquantized", action="store_true")
+    ap.add_argument("--no-graphs", action="store_true", help="eager per-layer decode (no CUDA graphs)")
     a = ap.parse_args()
     t0 = time.time()
     model = build_model(num_layers=a.layers, quantized=not a.unquantized, seed=a.seed)
     g = torch.Generator(device="cuda").manual_seed(a.seed + 1)
     prompt = torch.randint(0, model.config.vocab_size, (a.batch, a.context), generator=g, device="cuda")
-    generate(model, prompt[:, :16], 4)                      # warm-up (kernels, workspaces)
+    gen = generate if a.no_graphs else generate_graphed
+    gen(model, prompt[:, :16], 4)                           # warm-up (kernels, workspaces)
     st = {}
-    ids, per_tok = generate(model, prompt, a.new, stats=st)
+    ids, per_tok = gen(model, prompt, a.new, stats=st)
     print(json.dumps({"metric": "end-to-end greedy decode (c3)", "value": a.batch / per_tok, "unit": "tokens/s",
                       "ms_per_token": per_tok * 1e3, "prompt_ms": st["prompt_s"] * 1e3, "batch": a.batch, "context": a.context, "new_tokens": a.new,
-                      "layers": a.layers, "quantized": not a.unquantized, "weights": "random-init fp16",
+                      "layers": a.layers, "quantized": not a.unquantized, "cuda_graphs": not a.no_graphs, "weights": "random-init fp16",
                       "first_tokens": ids[0, :8].tolist(), "wall_s": time.time() - t0}))
 
 
