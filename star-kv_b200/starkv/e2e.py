@@ -200,14 +200,15 @@ def generate_graphed(model, prompt: torch.Tensor, new_tokens: int, capacity: int
         pool = g.pool()
         graphs.append(g)
     g_embed, g_pre, g_post, g_head = graphs[0], graphs[1:1 + len(layers)], graphs[1 + len(layers):-1], graphs[-1]
+    steps = [st.prepared_step(q_s, x_s, vs[i][0], vs[i][1], attn_s) for i, st in enumerate(states)]
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for s in range(new_tokens - 1):
         g_embed.replay()
-        for i, st in enumerate(states):
+        for i in range(len(states)):
             g_pre[i].replay()
-            st.step_from_hidden(q_s, x_s, vs[i][0], vs[i][1], out=attn_s)
+            steps[i]()
             g_post[i].replay()
         g_head.replay()
         out.append(tok_s.clone())

@@ -10,11 +10,12 @@ table and the workspace of one layer, and runs the step the reference runs in
 
 from __future__ import annotations
 
+import ctypes as C
 from typing import Optional, Sequence
 
 import torch
 
-from . import ops
+from . import _lib, ops
 
 
 def rope_inv_freq(theta: float, head_dim: int = 128, device=None) -> torch.Tensor:
@@ -72,6 +73,56 @@ class DecodeLayer:
             h = hidden.reshape(self.layout.batch, 1, -1)
             self.cache.append(torch.matmul(h, vs_k.T).contiguous(), torch.matmul(h, vs_v.T).contiguous())
         return self.attend(q_rot, mask=mask, out=out, events=events)
+
+    def prepared_step(self, q_rot: torch.Tensor, hidden: torch.Tensor, vs_k: torch.Tensor, vs_v: torch.Tensor,
+                      out: torch.Tensor):
+        """``step_from_hidden`` bound once to fixed buffers, for loops that reuse
+        the same tensors every step (e.g. between CUDA-graph replays): the C
+        argument blocks, the stream and the workspace are built here, and the
+        returned ``run()`` only sets the slot / token count and makes the two C
+        calls (``starkv_project_append``, ``starkv_decode_attention``) on the
+        stream current now.  Batches above ``FUSED_PROJECTION_MAX_BATCH`` use
+        ``step_from_hidden`` as is."""
+        if self.layout.batch > self.FUSED_PROJECTION_MAX_BATCH:
+            return lambda: self.step_from_hidden(q_rot, hidden, vs_k, vs_v, out=out)
+        L, c = self.layout, self.cache
+        dt = c.latent_dtype
+        H = hidden.shape[-1]
+        ops._require(hidden, "hidden", dt, L.batch * H)
+        ops._require(vs_k, "vs_k", dt, L.k_rank_total * H)
+        ops._require(vs_v, "vs_v", dt, L.v_rank_total * H)
+        ops._require(q_rot, "q", None, L.batch * L.num_q_heads * 128, align=4)
+        ops._require(out, "out", None, L.batch * L.num_q_heads * 128, align=4)
+        lib = _lib.load()
+        stream = ops._stream()
+        lay = C.byref(L)
+        pa_head = (lay, ops._ptr(hidden), H, ops._ptr(vs_k), ops._ptr(vs_v))
+        pa_tail = (ops._ptr(c.k_cache), ops._ptr(c.k_scales), ops._ptr(c.v_cache), ops._ptr(c.v_params), None, None,
+                   stream)
+        state = {}
+
+        def bind(T):
+            ws = ops.workspace(max(ops.workspace_size(L, min(L.capacity, T + 4096), self.num_splits),
+                                   ops.workspace_size(L, T, self.num_splits)), q_rot.device)
+            a = ops._decode_args(L, c, q_rot, self.k_u, self.v_u, self.inv_freq, self.scaling, T, None, out, ws,
+                                 self.num_splits)
+            state.update(ws=ws, a=a, ref=C.byref(a))
+
+        bind(c.length + 1)
+
+        def run():
+            if c.length >= L.capacity:
+                raise _lib.StarKVError("cache is full")
+            _lib.check(lib.starkv_project_append(*pa_head, c.length, *pa_tail), "starkv_project_append")
+            c.length += 1
+            a = state["a"]
+            a.num_tokens = c.length
+            rc = lib.starkv_decode_attention(lay, state["ref"], stream)
+            if rc == 4:                                  # workspace too small for this token count
+                bind(c.length)
+                rc = lib.starkv_decode_attention(lay, state["ref"], stream)
+            _lib.check(rc, "starkv_decode_attention")
+        return run
 
     def step(self, q_rot: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
              mask: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
