@@ -15,7 +15,11 @@
 namespace starkv {
 
 // ---- K: per-channel scales over the prefill + codes for the prefill tokens.
-// grid (Hkv, B), block 256.  k_lat: (B, T, k_rank_total) latent dtype.
+// grid (Hkv, B, Z), block 256.  k_lat: (B, T, k_rank_total) latent dtype.  Every
+// CTA of a (KV head, sequence) forms the same per-channel absmax over all T
+// tokens (the re-reads come from L2), CTA z == 0 writes the scales, and CTA z
+// quantises tokens [z*ceil(T/Z), (z+1)*ceil(T/Z)): the prompt's tokens spread
+// over many SMs instead of one CTA per head.
 template <typename LT>
 __global__ void __launch_bounds__(256) k_prefill_quant_kernel(const starkv_layout lay, const LT* __restrict__ k_lat,
                                                               int T, int8_t* __restrict__ k_cache,
@@ -41,16 +45,18 @@ __global__ void __launch_bounds__(256) k_prefill_quant_kernel(const starkv_layou
     for (int s = 1; s < 8; ++s) amax = fmaxf(amax, red[s][c]);
     __half h = __float2half_rn(__fdiv_rn(amax, 127.0f));
     if (__half2float(h) == 0.0f) h = __float2half_rn(1.0f);
-    k_scales[(int64_t)b * K + lay.k_col[kv] + c] = h;
+    if (blockIdx.z == 0) k_scales[(int64_t)b * K + lay.k_col[kv] + c] = h;
     sc[c] = __half2float(h);
   }
   __syncthreads();
-  for (int64_t e = threadIdx.x; e < (int64_t)T * r; e += blockDim.x) {
-    const int t = (int)(e / r), c = (int)(e % r);
-    float q = rintf(__fdiv_rn(to_f32(src[(int64_t)t * K + c]), sc[c]));
-    q = fminf(fmaxf(q, -127.f), 127.f);
-    k_cache[k_elem(lay, kv, b, t, c, 1)] = (int8_t)(int)q;
-  }
+  const int chunk = (T + gridDim.z - 1) / gridDim.z;
+  const int t0 = blockIdx.z * chunk, t1 = min(T, t0 + chunk);
+  for (int t = t0 + slot; t < t1; t += 8)
+    for (int c = col; c < r; c += 32) {
+      float q = rintf(__fdiv_rn(to_f32(src[(int64_t)t * K + c]), sc[c]));
+      q = fminf(fmaxf(q, -127.f), 127.f);
+      k_cache[k_elem(lay, kv, b, t, c, 1)] = (int8_t)(int)q;
+    }
 }
 
 // ---- K append with existing scales.  One thread per (b, t, channel of sum r).

@@ -4,6 +4,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <type_traits>
@@ -533,7 +534,10 @@ int starkv_quantize_prefill(const starkv_layout* lay, const void* k_lat, const v
   cudaStream_t st = (cudaStream_t)stream;
   const starkv_layout& l = *lay;
   if (!l.quantized) return starkv_append(lay, k_lat, v_lat, num_tokens, 0, k_cache, k_scales, v_cache, v_params, stream);
-  dim3 kg(l.num_kv_heads, l.batch);
+  // spread the prompt's tokens over about two waves of CTAs (at least 256 tokens each)
+  const int kz = std::max(1, std::min((num_tokens + 255) / 256,
+                                      (2 * 148 + l.num_kv_heads * l.batch - 1) / (l.num_kv_heads * l.batch)));
+  dim3 kg(l.num_kv_heads, l.batch, kz);
   switch (l.latent_dtype) {
     case STARKV_F16:
       k_prefill_quant_kernel<__half><<<kg, 256, 0, st>>>(l, (const __half*)k_lat, num_tokens, (int8_t*)k_cache, (__half*)k_scales);
