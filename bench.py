@@ -197,6 +197,82 @@ def run_c3(args):
         "prompt_ms": st["prompt_s"] * 1e3, "prompt_plus_decode_wall_s": wall}), flush=True)
 
 
+# ---------------------------------------------------------------- prompt attention
+def run_prefill(args):
+    """Prompt (prefill) attention, the library's tcgen05 causal flash-attention kernel
+    (``starkv_prefill_attention``) on the c3 model's attention shape: batch 1, 32 query /
+    32 KV heads x 128, ``--context`` prompt tokens (default 16384), fp16 q / k / v read
+    through (B, T, H, 128) views.  Inputs (3 x 134 MB at 16K) exceed L2.  ``value`` is
+    causal attention TFLOP/s (4 * T^2/2 * 128 * H per launch) on device-resident inputs;
+    ``e2e`` adds the pinned host -> device copy of q / k / v and the device -> host copy
+    of the output to every step; torch SDPA (cuDNN) on the same tensors is timed beside it."""
+    import torch
+    import torch.nn.functional as F
+    from starkv import ops
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference's prompt attention is torch SDPA on "
+                                                             "the GPU; it is timed beside this arm as sdpa_ms"}))
+        return
+    torch.cuda.set_device(0)
+    B, H, T = 1, 32, args.context or 16384
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q, k, v = (torch.randn(B, T, H, 128, generator=g, device="cuda").half().transpose(1, 2) for _ in range(3))
+    out = torch.empty(B, T, H, 128, dtype=torch.float16, device="cuda").transpose(1, 2)
+    sc = 128 ** -0.5
+    flops = 4.0 * B * H * (T * T / 2) * 128
+    W, K = max(args.warmup, 3), min(args.steps, 50)
+
+    def timed(fn, n):
+        for _ in range(W):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    with ClockSampler(0) as clk:
+        ms = timed(lambda: ops.prefill_attention(q, k, v, sc, out=out), K)
+    sdpa_ms = timed(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True, scale=sc), K)
+    # end to end: host tensors in pinned memory, copies inside the timed region
+    hq, hk, hv = (x.transpose(1, 2).contiguous().cpu().pin_memory() for x in (q, k, v))
+    hout = torch.empty(B, T, H, 128, dtype=torch.float16).pin_memory()
+    dq, dk, dv = (torch.empty_like(x, device="cuda") for x in (hq, hk, hv))
+    dout = torch.empty(B, T, H, 128, dtype=torch.float16, device="cuda")
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        ops.prefill_attention(dq.transpose(1, 2), dk.transpose(1, 2), dv.transpose(1, 2), sc,
+                              out=dout.transpose(1, 2))
+        hout.copy_(dout, non_blocking=True)
+    e2e_ms = timed(e2e_step, max(3, K // 5))
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak, kind = float(json.load(f)["bf16_tflops"]), "measured (cuBLAS bf16 burst; fp16 runs at the same rate)"
+    except Exception:
+        peak, kind = 1590.0, "fallback"
+    tf = flops / ms / 1e9
+    print(json.dumps({
+        "metric": "prompt attention TFLOP/s (causal, c3 attention shape)", "value": tf, "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp16", "data": "synthetic (random q / k / v)",
+        "config": {"workload": "prefill: causal attention of one layer, batch 1, 32 heads x 128",
+                   "context": T, "l2": ("inputs larger than L2" if 3 * B * T * H * 256 > 126e6 else
+                                        "inputs fit in L2 (no flush)") + " (3 x %.0f MB)" % (B * T * H * 256 / 1e6)},
+        "roofline": {"kernel": "prefill_attn2_kernel<__half>", "bound": "tensor", "achieved": tf, "peak": peak,
+                     "unit": "TFLOP/s", "frac": tf / peak, "peak_kind": kind, "traffic": None},
+        "sdpa_ms": sdpa_ms, "sdpa_tflops": flops / sdpa_ms / 1e9, "gpu_launches": K,
+        "e2e": {"value": flops / e2e_ms / 1e9, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": 3 * B * T * H * 256, "d2h_bytes_per_step": B * T * H * 256,
+                "api": "starkv.ops.prefill_attention (C ABI starkv_prefill_attention)"},
+        "clocks": clk.summary()}), flush=True)
+
+
 # ---------------------------------------------------------------- GPU arm
 def main():
     ap = argparse.ArgumentParser()
@@ -221,6 +297,9 @@ def main():
         over["batch"] = args.batch
     if args.config == "c3":
         run_c3(args)
+        return
+    if args.config == "prefill":
+        run_prefill(args)
         return
     spec = make_spec(args.config, seed=0, **over)
 
