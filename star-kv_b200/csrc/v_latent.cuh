@@ -331,13 +331,30 @@ __global__ void __launch_bounds__(128) combine_kernel(const __grid_constant__ Co
   }
   __syncthreads();
   const float inv = s_inv;
-  for (int c = tid; c < r; c += 128) {
-    float s = 0.f;
-    const float* src = p.partial + ((int64_t)b * Hq + qh) * p.nsplit * p.rv_max + c;
-#pragma unroll 4
-    for (int k = 0; k < p.nsplit; ++k) s += src[(int64_t)k * p.rv_max];
-    o_lat[c] = s * inv;
+  // split sums: warp w adds splits w, w + 4, ... for channels lane + 32i (coalesced
+  // rows, up to eight independent loads in flight per lane), then the four warps'
+  // sums meet in shared memory in a fixed order (the result does not depend on timing)
+  __shared__ float part[4][kVMaxRank];
+  {
+    const int w = tid >> 5, ln = tid & 31;
+    const float* base = p.partial + ((int64_t)b * Hq + qh) * p.nsplit * p.rv_max;
+    for (int c0 = 0; c0 < r; c0 += 256) {
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int k = w; k < p.nsplit; k += 4) {
+        const float* src = base + (int64_t)k * p.rv_max + c0 + ln;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (c0 + ln + 32 * i < r) acc[i] += src[32 * i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (c0 + ln + 32 * i < r) part[w][c0 + ln + 32 * i] = acc[i];
+    }
   }
+  __syncthreads();
+  for (int c = tid; c < r; c += 128) o_lat[c] = (((part[0][c] + part[1][c]) + part[2][c]) + part[3][c]) * inv;
   __syncthreads();
   // out[d] = sum_c o_lat[c] * U_v[kv * 128 + d, vcol + c]: warp w takes the rows
   // d = w, w + 4, ...; lane l the 8 consecutive channels 8l + 256k of the row (one
