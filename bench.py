@@ -347,11 +347,15 @@ def main():
     out = torch.empty(B, hq, 128, dtype=st.q.dtype, device=dev)
     gathered = torch.empty(world * B, hq, 128, dtype=st.q.dtype, device=dev) if world > 1 else None
 
-    def step(events=None):
+    def step(events=None, gev=None):
         layer.cache.length = L                      # the step rewrites slot L and attends 0..L
         layer.step(st.q, st.k_new, st.v_new, out=out, events=events)
         if world > 1:
+            if gev is not None:
+                gev[0].record()
             sd.gather_heads(out, buffer=gathered)
+            if gev is not None:
+                gev[1].record()
 
     for _ in range(args.warmup):
         step()
@@ -360,8 +364,9 @@ def main():
 
     K = args.steps
     kev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    gev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(K)] if world > 1 else None
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for e in [x for row in kev for x in row] + [t0, t1]:
+    for e in [x for row in kev + (gev or []) for x in row] + [t0, t1]:
         e.record()                                  # create the CUDA events before the timed region
     if world > 1:
         dist.barrier()
@@ -369,7 +374,7 @@ def main():
     with ClockSampler(local) as clk:
         t0.record()
         for i in range(K):
-            step(kev[i])
+            step(kev[i], gev[i] if gev else None)
         t1.record()
         torch.cuda.synchronize()
     assert ops.read_device_error(device=dev) == 0, "a device wait timed out in the timed region"
@@ -379,10 +384,11 @@ def main():
     k_ms = sum(e[0].elapsed_time(e[1]) for e in kev) / K
     v_ms = sum(e[1].elapsed_time(e[2]) for e in kev) / K
     c_ms = sum(e[2].elapsed_time(e[3]) for e in kev) / K
+    g_ms = sum(e[0].elapsed_time(e[1]) for e in gev) / K if gev else 0.0
     if world > 1:
-        t = torch.tensor([ms, k_ms, v_ms, c_ms], device=dev)
+        t = torch.tensor([ms, k_ms, v_ms, c_ms, g_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, k_ms, v_ms, c_ms = t.tolist()
+        ms, k_ms, v_ms, c_ms, g_ms = t.tolist()
 
     # ---- e2e through the public step API with host buffers
     e2e = None
@@ -481,6 +487,8 @@ def main():
         "hbm_gbs_per_gpu": rank_bytes / (ms / 1e3) / 1e9,
         "hbm_frac_step": (rank_bytes / (ms / 1e3) / 1e9) / peak,
         "kernels_ms": {"k_logits": k_ms, "v_latent": v_ms, "combine": c_ms},
+        "allgather_ms": g_ms if world > 1 else None,     # NCCL all-gather, including the wait for the slowest rank
+        "value_without_allgather": (spec.batch / ((ms - g_ms) / 1e3)) if world > 1 else None,
         "v_kernel_gbs": v_bytes / (v_ms / 1e3) / 1e9,
         "roofline": roofline,
         "gpu_launches": 6 * K,                    # append (2), W pre-pass, K, V, combine
